@@ -1,0 +1,849 @@
+// Paged-attention decode kernels for B200 (sm_100a): FP16 and per-token INT8 KV caches.
+//
+// Design (one kernel family, three modes, see pa_internal.h):
+//  * A warp is an independent decode engine. It owns a DEPTH-deep ring of shared-memory
+//    stages; its lane 0 fills them with TMA copies (the K tile through a tensor map with the
+//    128-byte swizzle, V and the per-token scales through 1-D bulk copies or tensor maps) and
+//    the whole warp consumes them. A stage holds one 16-token "subpage" of one
+//    (block, kv-head) page: K and V tiles plus, for INT8, 16 K scales and 16 V scales.
+//  * Every CTA first scans context_lens (all sequences, kept in shared memory) and then the
+//    flattened work list "sequence x kv-head x head-tile x subpage" is cut into equal page
+//    ranges, one per warp (stream mode), so ragged batches and long contexts are balanced.
+//    A warp whose range cuts a segment (one sequence x kv-head) writes an un-normalised
+//    partial (O, m, l); the last warp to finish a segment (atomic arrival counter) merges the
+//    partials with the log-sum-exp rule and writes the fp16 output. Split mode instead snaps
+//    the ranges to 512-token splits and writes one partial per split for the reduce kernel
+//    (the split-K pair); partial mode writes one merged partial per segment (cross-GPU).
+//  * All q heads of a GQA group share one pass over the K/V page: QK^T and PV run on the
+//    tensor cores (mma.sync m16n8k16, f16 in / f32 accumulate) with heads on the MMA rows
+//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8 K/V bytes are
+//    unpacked to exact fp16 integers in registers; the per-token K scale multiplies the
+//    integer dot product and the per-token V scale is folded into the softmax weight
+//    (the dequant fusion of kernels/paged_attention_v5_warp_int8.cu:82-85,101-108).
+//
+// Arithmetic follows the reference decode (tests/paged_decode_attn.py:4-49 and the split-K
+// pair kernels/paged_attention_v4_splitk.cu:28-187): softmax(scale * q.k) v over the tokens
+// of each sequence gathered through block_table, with online (running max) softmax and the
+// split merge  m = max m_s,  l = sum l_s e^{m_s - m},  o = sum o_s e^{m_s - m} / l.
+// Scores are kept in log2 units (scale * log2 e) so the exponentials are exp2.
+
+#include "pa_common.cuh"
+#include "pa_internal.h"
+
+#include <cstdio>
+
+namespace pa {
+namespace {
+
+// Per-lane chunk (8 head-dim values) used by load `si` of lane group position r.
+// INT8 K tiles (128-byte rows = one chunk, 16 tokens x 8 bytes) and FP16 K tiles (two
+// 128-byte rows per chunk) are stored with the TMA 128-byte swizzle; these chunk orders make
+// every shared-memory K load of a warp hit 32 distinct banks.
+__device__ __forceinline__ int chunk_i8(int r, int si) {
+  return ((r & 1) | ((r & 2) << 1)) + ((si >> 1) << 3) + ((si & 1) << 1);
+}
+__device__ __forceinline__ int chunk_f16(int r, int si) { return r + 4 * si; }
+
+template <int KVK, int D, int GT, int DEPTH, int WARPS>
+struct Tile {
+  static constexpr bool I8 = KVK == 1;
+  static constexpr int ELEM = I8 ? 1 : 2;
+  static constexpr int KT = D * kSubTokens * ELEM;  // K tile bytes
+  static constexpr int VT = D * kSubTokens * ELEM;  // V tile bytes
+  static constexpr int ST = I8 ? 128 : 0;           // 16 K scales + 16 V scales
+  static constexpr uint32_t TX = KT + VT + ST;      // bytes per stage
+  static constexpr int NS = D / 32;                 // 8-value K loads per token per lane
+  static constexpr int MT = D / 16;                 // PV m-tiles (head_dim rows)
+  static constexpr int NT = GT / 8;                 // PV n-tiles (heads)
+  static constexpr int SLOT = (D + 2) * GT;         // partial slot floats
+  static constexpr size_t SMEM = 1024 + (size_t)WARPS * DEPTH * (KT + VT + ST) +
+                                 (size_t)WARPS * DEPTH * 8;
+};
+
+// ---------------------------------------------------------------------------------------
+// Warp-level log-sum-exp merge of `np` partial slots into either fp16 output rows
+// (out_rows[h * D + d]) or one merged partial slot (out_slot). Slot layout: O[D][GT], m[GT],
+// l[GT]; lane owns head_dim rows [lane*D/32, (lane+1)*D/32).
+// ---------------------------------------------------------------------------------------
+template <int D, int GT, typename PieceFn>
+__device__ __forceinline__ void combine_pieces(PieceFn piece, int np, int lane, int hcnt,
+                                               __half* out_rows, float* out_slot,
+                                               int* status) {
+  constexpr int DPL = D / 32;
+  float M[GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) M[h] = neg_inf();
+  for (int k = 0; k < np; ++k) {
+    const float* sl = piece(k);
+#pragma unroll
+    for (int h = 0; h < GT; ++h) M[h] = fmaxf(M[h], __ldcg(sl + D * GT + h));
+  }
+  float L[GT];
+  float acc[DPL][GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) {
+    L[h] = 0.f;
+#pragma unroll
+    for (int dd = 0; dd < DPL; ++dd) acc[dd][h] = 0.f;
+  }
+  for (int k = 0; k < np; ++k) {
+    const float* sl = piece(k);
+    float wgt[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+      const float mk = __ldcg(sl + D * GT + h);
+      wgt[h] = (M[h] == neg_inf()) ? 0.f : ex2(mk - M[h]);
+      L[h] += wgt[h] * __ldcg(sl + D * GT + GT + h);
+    }
+    const float4* rows = reinterpret_cast<const float4*>(sl + lane * DPL * GT);
+#pragma unroll
+    for (int dd = 0; dd < DPL; ++dd) {
+#pragma unroll
+      for (int h4 = 0; h4 < GT / 4; ++h4) {
+        const float4 v = __ldcg(rows + dd * (GT / 4) + h4);
+        acc[dd][4 * h4 + 0] += wgt[4 * h4 + 0] * v.x;
+        acc[dd][4 * h4 + 1] += wgt[4 * h4 + 1] * v.y;
+        acc[dd][4 * h4 + 2] += wgt[4 * h4 + 2] * v.z;
+        acc[dd][4 * h4 + 3] += wgt[4 * h4 + 3] * v.w;
+      }
+    }
+  }
+  if (out_rows != nullptr) {
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+      if (h < hcnt) {
+        float inv = 0.f;
+        if (L[h] > 0.f) {
+          inv = 1.f / L[h];
+        } else if (lane == 0) {
+          flag_error(status, PA_ERR_EMPTY_CONTEXT);
+        }
+        __half tmp[DPL];
+#pragma unroll
+        for (int dd = 0; dd < DPL; ++dd) tmp[dd] = __float2half_rn(acc[dd][h] * inv);
+        __half* dst = out_rows + (size_t)h * D + lane * DPL;
+        if constexpr (DPL == 4) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(tmp);
+        } else {
+#pragma unroll
+          for (int dd = 0; dd < DPL; ++dd) dst[dd] = tmp[dd];
+        }
+      }
+    }
+  } else {
+    float4* rows = reinterpret_cast<float4*>(out_slot + lane * DPL * GT);
+#pragma unroll
+    for (int dd = 0; dd < DPL; ++dd) {
+#pragma unroll
+      for (int h4 = 0; h4 < GT / 4; ++h4) {
+        rows[dd * (GT / 4) + h4] =
+            make_float4(acc[dd][4 * h4], acc[dd][4 * h4 + 1], acc[dd][4 * h4 + 2],
+                        acc[dd][4 * h4 + 3]);
+      }
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int h = 0; h < GT; ++h) {
+        out_slot[D * GT + h] = M[h];
+        out_slot[D * GT + GT + h] = L[h];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// The decode kernel.
+// ---------------------------------------------------------------------------------------
+template <int KVK, int D, int GT, int DEPTH, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    decode_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v,
+                  const __grid_constant__ CUtensorMap tm_ks,
+                  const __grid_constant__ CUtensorMap tm_vs) {
+  using C = Tile<KVK, D, GT, DEPTH, WARPS>;
+  constexpr bool I8 = C::I8;
+  constexpr int NS = C::NS;
+  constexpr int MT = C::MT;
+  constexpr int NT = C::NT;
+  constexpr int SLOT = C::SLOT;
+  constexpr int NTHR = WARPS * 32;
+
+  __shared__ int s_pre[kBMax + 1];
+  __shared__ int s_ctx[kBMax];
+  __shared__ int s_tmp[32];
+  __shared__ int s_empty;
+  extern __shared__ __align__(16) uint8_t dsm_raw[];
+
+  uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
+  uint8_t* k_tiles = dsm;
+  uint8_t* v_tiles = k_tiles + WARPS * DEPTH * C::KT;
+  uint8_t* s_tiles = v_tiles + WARPS * DEPTH * C::VT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_tiles + WARPS * DEPTH * C::ST);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;  // MMA group (row / column index)
+  const int r = lane & 3;   // position inside the group
+  uint64_t* wbar = bars + warp * DEPTH;
+
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < DEPTH; ++s) mbar_init(&wbar[s], 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x == 0) {
+    s_empty = 0;
+    prefetch_tensormap(&tm_k);
+    if (!a.bulk) {
+      prefetch_tensormap(&tm_v);
+      if constexpr (I8) {
+        prefetch_tensormap(&tm_ks);
+        prefetch_tensormap(&tm_vs);
+      }
+    }
+  }
+
+  // ---- 1. Scan of per-sequence page counts (all CTAs, identical result) -------------------
+  const int SEGS = a.KVH * a.HT;
+  const int cap = a.max_blocks * a.bs;
+  int carry = 0;
+  __syncthreads();
+  for (int base = 0; base < a.B; base += NTHR) {
+    const int b = base + threadIdx.x;
+    int w = 0;
+    if (b < a.B) {
+      int c = __ldg(a.context_lens + b);
+      if (c < 1) {
+        if (blockIdx.x == 0 && a.mode != kModePartial) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
+        if (blockIdx.x == 0 && c < 0) flag_error(a.status, PA_ERR_CONTEXT_RANGE);
+        s_empty = 1;
+        c = 0;
+      }
+      if (c > cap) {
+        if (blockIdx.x == 0) flag_error(a.status, PA_ERR_CONTEXT_RANGE);
+        c = cap;
+      }
+      s_ctx[b] = c;
+      w = ((c + kSubTokens - 1) / kSubTokens) * SEGS;
+    }
+    int v = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += t;
+    }
+    if (lane == 31) s_tmp[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int t = (lane < WARPS) ? s_tmp[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += u;
+      }
+      if (lane < WARPS) s_tmp[lane] = t;
+    }
+    __syncthreads();
+    if (b < a.B) s_pre[b] = carry + (warp ? s_tmp[warp - 1] : 0) + v - w;
+    carry += s_tmp[WARPS - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) s_pre[a.B] = carry;
+  __syncthreads();
+  const int T = carry;
+
+  // Sequences with no tokens: zero output (stream) or an empty partial (partial mode).
+  if (blockIdx.x == 0 && s_empty) {
+    if (a.mode == kModeStream) {
+      const int per_b = a.H * D / 8;
+      for (int i = threadIdx.x; i < a.B * per_b; i += NTHR) {
+        const int b = i / per_b;
+        if (s_ctx[b] == 0)
+          reinterpret_cast<uint4*>(a.out + (size_t)b * a.H * D)[i - b * per_b] =
+              make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else if (a.mode == kModePartial) {
+      for (int i = threadIdx.x; i < a.B * SEGS * SLOT; i += NTHR) {
+        const int segid = i / SLOT;
+        const int b = segid / SEGS;
+        if (s_ctx[b] == 0) {
+          const int k = i - segid * SLOT;
+          a.part_out[i] = (k >= D * GT && k < D * GT + GT) ? neg_inf() : 0.f;
+        }
+      }
+    }
+  }
+  if (T == 0) return;
+
+  auto pages_of = [&](int b) { return (s_ctx[b] + kSubTokens - 1) / kSubTokens; };
+  // Flattened page index -> (sequence, segment inside the sequence, subpage).
+  auto locate = [&](int p, int& b, int& seg, int& sp) {
+    int lo = 0, hi = a.B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_pre[mid] <= p) lo = mid; else hi = mid - 1;
+    }
+    b = lo;
+    const int rel = p - s_pre[b];
+    const int pg = pages_of(b);
+    seg = rel / pg;
+    sp = rel - seg * pg;
+  };
+  // Smallest split start >= p (split mode).
+  auto snap = [&](long long p) -> long long {
+    if (p >= T) return T;
+    int b, seg, sp;
+    locate((int)p, b, seg, sp);
+    const int pg = pages_of(b);
+    const int sp2 = (sp + kSplitPages - 1) / kSplitPages * kSplitPages;
+    if (sp2 >= pg) return (long long)s_pre[b] + (long long)(seg + 1) * pg;
+    return (long long)s_pre[b] + (long long)seg * pg + sp2;
+  };
+
+  // ---- 2. This warp's page range ------------------------------------------------------------
+  const long long Wt = min((long long)a.total_warps, (long long)T);
+  const int wg = blockIdx.x * WARPS + warp;
+  if (wg >= Wt) return;
+  long long p0 = (long long)wg * T / Wt;
+  long long p1 = (long long)(wg + 1) * T / Wt;
+  if (a.mode == kModeSplit) {
+    p0 = snap(p0);
+    p1 = snap(p1);
+  }
+  const int n = (int)(p1 - p0);
+  if (n <= 0) return;
+
+  // ---- 3. Producer: block ids for 32 upcoming pages live one per lane -----------------------
+  struct PB { int blk, kvh, sub; };
+  auto batch_info = [&](int jbase) {
+    PB o{0, 0, 0};
+    const int j = jbase + lane;
+    if (j < n) {
+      int b, seg, sp;
+      locate((int)(p0 + j), b, seg, sp);
+      o.kvh = seg / a.HT;
+      const int bi = sp / a.subs;
+      o.sub = sp - bi * a.subs;
+      o.blk = __ldg(a.block_table + (size_t)b * a.max_blocks + bi);
+    }
+    return o;
+  };
+  PB cur = batch_info(0);
+  PB nxt = batch_info(32);
+
+  auto issue = [&](int j) {
+    if (j > 0 && (j & 31) == 0) {
+      cur = nxt;
+      nxt = batch_info(j + 32);
+    }
+    const int src = j & 31;
+    int blk = __shfl_sync(0xffffffffu, cur.blk, src);
+    const int kvh = __shfl_sync(0xffffffffu, cur.kvh, src);
+    const int sub = __shfl_sync(0xffffffffu, cur.sub, src);
+    if (lane == 0) {
+      if (blk < 0 || blk >= a.NB) {
+        flag_error(a.status, PA_ERR_BLOCK_ID);
+        blk = 0;
+      }
+      const int row = blk * a.KVH + kvh;
+      const int s = j % DEPTH;
+      uint64_t* bar = &wbar[s];
+      uint8_t* kd = k_tiles + (warp * DEPTH + s) * C::KT;
+      uint8_t* vd = v_tiles + (warp * DEPTH + s) * C::VT;
+      mbar_arrive_expect_tx(bar, C::TX);
+      if constexpr (I8) {
+        tma_load_3d(kd, &tm_k, bar, sub * 128, 0, row);
+      } else {
+        tma_load_4d(kd, &tm_k, bar, 0, sub * 2, 0, row);
+      }
+      if (a.bulk) {
+        bulk_g2s(vd, a.v_base + (size_t)row * C::VT, C::VT, bar);
+        if constexpr (I8) {
+          uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
+          bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
+          bulk_g2s(sd + 64, a.vs_base + (size_t)row * kSubTokens, 64, bar);
+        }
+      } else {
+        tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
+        if constexpr (I8) {
+          uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
+          tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
+          tma_load_2d(sd + 64, &tm_vs, bar, sub * kSubTokens, row);
+        }
+      }
+    }
+  };
+
+  const int npro = n < DEPTH ? n : DEPTH;
+  __syncwarp();
+  for (int j = 0; j < npro; ++j) issue(j);
+  int issued = npro;
+
+  // ---- 4. Consumer state ---------------------------------------------------------------------
+  int cb, cseg, csp;
+  locate((int)p0, cb, cseg, csp);
+  int cpg = pages_of(cb);
+  int piece_sp0 = csp;
+  const float qs = a.qk_scale_log2;
+
+  uint4 qa[NS], qb[NS], qna[NS], qnb[NS];
+  int q_b = -1, q_seg = -1, qn_b = -1, qn_seg = -1;
+
+  auto load_q = [&](int b, int seg, uint4 (&xa)[NS], uint4 (&xb)[NS]) {
+    const int kvh = seg / a.HT;
+    const int ht = seg - kvh * a.HT;
+    const int hl = ht * GT + g;
+    const __half* qrow = a.q + ((size_t)b * a.H + (size_t)kvh * a.G + hl) * D;
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const int c = I8 ? chunk_i8(r, si) : chunk_f16(r, si);
+      xa[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
+                          : make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (GT == 16) {
+        xb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
+                                : make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        xb[si] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  };
+
+  float m0 = neg_inf(), l0 = 0.f, m1 = neg_inf(), l1 = 0.f;
+  float oacc[MT][NT][4];
+
+  int jfail = -1;
+  for (int j = 0; j < n; ++j) {
+    const int s = j % DEPTH;
+    const bool split = (a.mode == kModeSplit);
+    const bool first = (j == 0) || (split ? (csp % kSplitPages == 0) : (csp == 0));
+    const bool last = (j == n - 1) || (csp == cpg - 1) ||
+                      (split && (csp % kSplitPages) == kSplitPages - 1);
+    if (first) {
+      if (q_b != cb || q_seg != cseg) {
+        if (qn_b == cb && qn_seg == cseg) {
+#pragma unroll
+          for (int si = 0; si < NS; ++si) {
+            qa[si] = qna[si];
+            qb[si] = qnb[si];
+          }
+        } else {
+          load_q(cb, cseg, qa, qb);
+        }
+        q_b = cb;
+        q_seg = cseg;
+      }
+      m0 = neg_inf();
+      l0 = 0.f;
+      m1 = neg_inf();
+      l1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) oacc[i][nt][e] = 0.f;
+      piece_sp0 = csp;
+    }
+    if (last && j + 1 < n) {
+      // Prefetch q of the next segment so the next piece does not wait on it.
+      int nb = cb, nseg = cseg, nsp = csp + 1;
+      if (nsp == cpg) {
+        nsp = 0;
+        if (++nseg == SEGS) {
+          nseg = 0;
+          do { ++nb; } while (pages_of(nb) == 0);
+        }
+      }
+      if ((nb != cb || nseg != cseg) && (nb != qn_b || nseg != qn_seg)) {
+        load_q(nb, nseg, qna, qnb);
+        qn_b = nb;
+        qn_seg = nseg;
+      }
+    }
+
+    if (!mbar_wait_bounded(&wbar[s], (uint32_t)(j / DEPTH) & 1u, a.status)) {
+      jfail = j;
+      break;
+    }
+
+    // ---- one 16-token subpage -----------------------------------------------------------------
+    {
+      const int valid = min(kSubTokens, s_ctx[cb] - csp * kSubTokens);
+      const uint32_t kb = smem_u32(k_tiles + (warp * DEPTH + s) * C::KT);
+      const uint32_t vb = smem_u32(v_tiles + (warp * DEPTH + s) * C::VT);
+      const uint32_t sb = I8 ? smem_u32(s_tiles + (warp * DEPTH + s) * C::ST) : 0u;
+
+      // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n).
+      float sacc[2][4];
+#pragma unroll
+      for (int jt = 0; jt < 2; ++jt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sacc[jt][e] = 0.f;
+#pragma unroll
+      for (int si = 0; si < NS; ++si) {
+#pragma unroll
+        for (int jt = 0; jt < 2; ++jt) {
+          const int tau = 4 * (g >> 1) + (g & 1) + 2 * jt;
+          uint32_t b0a, b1a, b0b, b1b;
+          if constexpr (I8) {
+            const int c = chunk_i8(r, si);
+            const uint2 kw =
+                lds64(kb + c * 128 + ((((tau >> 1) ^ (c & 7)) << 4) | ((tau & 1) << 3)));
+            i8x4_to_f16x2x2(kw.x, b0a, b1a);
+            i8x4_to_f16x2x2(kw.y, b0b, b1b);
+          } else {
+            const int c = chunk_f16(r, si);
+            const int row = 2 * c + (tau >> 3);
+            const uint4 kw = lds128(kb + row * 128 + (((tau & 7) ^ (row & 7)) << 4));
+            b0a = kw.x;
+            b1a = kw.y;
+            b0b = kw.z;
+            b1b = kw.w;
+          }
+          mma_16816(sacc[jt], qa[si].x, qb[si].x, qa[si].y, qb[si].y, b0a, b1a);
+          mma_16816(sacc[jt], qa[si].z, qb[si].z, qa[si].w, qb[si].w, b0b, b1b);
+        }
+      }
+
+      // Scores of tokens 4r..4r+3 for heads g (x) and g+8 (y), in log2 units.
+      float x[4] = {sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]};
+      float y[4] = {sacc[0][2], sacc[0][3], sacc[1][2], sacc[1][3]};
+      float ksc[4] = {qs, qs, qs, qs};
+      if constexpr (I8) {
+        const float4 ks = lds128f(sb + 16 * r);
+        ksc[0] = ks.x * qs;
+        ksc[1] = ks.y * qs;
+        ksc[2] = ks.z * qs;
+        ksc[3] = ks.w * qs;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[e] *= ksc[e];
+        if constexpr (NT == 2) y[e] *= ksc[e];
+      }
+      if (valid < kSubTokens) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (4 * r + e >= valid) {
+            x[e] = neg_inf();
+            y[e] = neg_inf();
+          }
+        }
+      }
+      float tm0 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 1));
+      tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 2));
+      const float mn0 = fmaxf(m0, tm0);
+      float mn1 = m1;
+      if constexpr (NT == 2) {
+        float tm1 = fmaxf(fmaxf(y[0], y[1]), fmaxf(y[2], y[3]));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 1));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 2));
+        mn1 = fmaxf(m1, tm1);
+      }
+      if (__any_sync(0xffffffffu, (mn0 > m0) || (mn1 > m1))) {
+        const float c0 = ex2(m0 - mn0);
+        l0 *= c0;
+        m0 = mn0;
+        const float ca = __shfl_sync(0xffffffffu, c0, 8 * r);
+        const float cb2 = __shfl_sync(0xffffffffu, c0, 8 * r + 4);
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          oacc[i][0][0] *= ca;
+          oacc[i][0][1] *= cb2;
+          oacc[i][0][2] *= ca;
+          oacc[i][0][3] *= cb2;
+        }
+        if constexpr (NT == 2) {
+          const float c1 = ex2(m1 - mn1);
+          l1 *= c1;
+          m1 = mn1;
+          const float cc = __shfl_sync(0xffffffffu, c1, 8 * r);
+          const float cd = __shfl_sync(0xffffffffu, c1, 8 * r + 4);
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            oacc[i][1][0] *= cc;
+            oacc[i][1][1] *= cd;
+            oacc[i][1][2] *= cc;
+            oacc[i][1][3] *= cd;
+          }
+        }
+      }
+      float p[4], pv[4], py[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        p[e] = ex2(x[e] - m0);
+        l0 += p[e];
+        pv[e] = p[e];
+        if constexpr (NT == 2) {
+          py[e] = ex2(y[e] - m1);
+          l1 += py[e];
+        } else {
+          py[e] = 0.f;
+        }
+      }
+      if constexpr (I8) {
+        const float4 vs = lds128f(sb + 64 + 16 * r);
+        const float vsc[4] = {vs.x, vs.y, vs.z, vs.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool ok = (4 * r + e) < valid;
+          pv[e] = ok ? p[e] * vsc[e] : 0.f;
+          if constexpr (NT == 2) py[e] = ok ? py[e] * vsc[e] : 0.f;
+        }
+      }
+      const uint32_t pb0 = pack_f16x2(pv[0], pv[1]);
+      const uint32_t pb1 = pack_f16x2(pv[2], pv[3]);
+      const uint32_t pc0 = pack_f16x2(py[0], py[1]);
+      const uint32_t pc1 = pack_f16x2(py[2], py[3]);
+
+      // O^T += V^T P^T : rows = head_dim (16 per m-tile), columns = heads.
+      uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
+      if (!I8 && valid < kSubTokens) {
+        mlo = ((4 * r < valid) ? 0x0000ffffu : 0u) | ((4 * r + 1 < valid) ? 0xffff0000u : 0u);
+        mhi = ((4 * r + 2 < valid) ? 0x0000ffffu : 0u) | ((4 * r + 3 < valid) ? 0xffff0000u : 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        uint32_t a0, a1, a2, a3;
+        if constexpr (I8) {
+          const uint32_t wa = lds32(vb + (16 * i + g) * 16 + 4 * r);
+          const uint32_t wb = lds32(vb + (16 * i + g + 8) * 16 + 4 * r);
+          i8x4_to_f16x2x2(wa, a0, a2);
+          i8x4_to_f16x2x2(wb, a1, a3);
+        } else {
+          const uint2 wa = lds64(vb + ((16 * i + g) * 16 + 4 * r) * 2);
+          const uint2 wb = lds64(vb + ((16 * i + g + 8) * 16 + 4 * r) * 2);
+          a0 = wa.x & mlo;
+          a2 = wa.y & mhi;
+          a1 = wb.x & mlo;
+          a3 = wb.y & mhi;
+        }
+        mma_16816(oacc[i][0], a0, a1, a2, a3, pb0, pb1);
+        if constexpr (NT == 2) mma_16816(oacc[i][1], a0, a1, a2, a3, pc0, pc1);
+      }
+    }
+
+    // Release the stage and refill it with the page DEPTH ahead.
+    __syncwarp();
+    if (j + DEPTH < n) {
+      if (lane == 0) fence_proxy_async_smem();
+      issue(j + DEPTH);
+      ++issued;
+    }
+
+    if (last) {
+      // ---- piece epilogue ---------------------------------------------------------------------
+      float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+      lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
+      float lt1 = 0.f;
+      if constexpr (NT == 2) {
+        lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+        lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
+      }
+      const int segid = cb * SEGS + cseg;
+      const int kvh = cseg / a.HT;
+      const int ht = cseg - kvh * a.HT;
+      const int hbase = kvh * a.G + ht * GT;
+      const int hcnt = min(GT, a.G - ht * GT);
+
+      auto write_slot = [&](float* slot) {
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            *reinterpret_cast<float2*>(slot + (16 * i + g) * GT + nt * 8 + 2 * r) =
+                make_float2(oacc[i][nt][0], oacc[i][nt][1]);
+            *reinterpret_cast<float2*>(slot + (16 * i + g + 8) * GT + nt * 8 + 2 * r) =
+                make_float2(oacc[i][nt][2], oacc[i][nt][3]);
+          }
+        }
+        if (r == 0) {
+          slot[D * GT + g] = m0;
+          slot[D * GT + GT + g] = lt0;
+          if constexpr (NT == 2) {
+            slot[D * GT + 8 + g] = m1;
+            slot[D * GT + GT + 8 + g] = lt1;
+          }
+        }
+      };
+
+      if (split) {
+        write_slot(a.part + ((size_t)segid * a.s_max + piece_sp0 / kSplitPages) * SLOT);
+      } else if (piece_sp0 == 0 && csp == cpg - 1) {
+        // The whole segment was this warp's: normalise and store directly.
+        if (a.mode == kModeStream) {
+          const float inv0 = 1.f / lt0;
+          const float ia = __shfl_sync(0xffffffffu, inv0, 8 * r);
+          const float ib = __shfl_sync(0xffffffffu, inv0, 8 * r + 4);
+          float ic = 0.f, id = 0.f;
+          if constexpr (NT == 2) {
+            const float inv1 = 1.f / lt1;
+            ic = __shfl_sync(0xffffffffu, inv1, 8 * r);
+            id = __shfl_sync(0xffffffffu, inv1, 8 * r + 4);
+          }
+          __half* ob = a.out + ((size_t)cb * a.H + hbase) * D;
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const int h = nt * 8 + 2 * r;
+              const float fa = nt ? ic : ia;
+              const float fb = nt ? id : ib;
+              if (h < hcnt) {
+                ob[(size_t)h * D + 16 * i + g] = __float2half_rn(oacc[i][nt][0] * fa);
+                ob[(size_t)h * D + 16 * i + g + 8] = __float2half_rn(oacc[i][nt][2] * fa);
+              }
+              if (h + 1 < hcnt) {
+                ob[(size_t)(h + 1) * D + 16 * i + g] = __float2half_rn(oacc[i][nt][1] * fb);
+                ob[(size_t)(h + 1) * D + 16 * i + g + 8] = __float2half_rn(oacc[i][nt][3] * fb);
+              }
+            }
+          }
+        } else {
+          write_slot(a.part_out + (size_t)segid * SLOT);
+        }
+      } else {
+        // A piece of a segment shared with neighbouring warps.
+        write_slot(a.part + ((size_t)wg * 2 + (piece_sp0 == 0 ? 1 : 0)) * SLOT);
+        __threadfence();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+          __threadfence();
+          old = atomicAdd(a.counters + segid, 1);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        const long long s_start = (long long)s_pre[cb] + (long long)cseg * cpg;
+        const long long s_end = s_start + cpg;
+        const int wf = (int)(((s_start + 1) * Wt - 1) / T);
+        const int wl = (int)((s_end * Wt - 1) / T);
+        const int np = wl - wf + 1;
+        if (old == np - 1) {
+          __threadfence();
+          auto piece = [&](int k) -> const float* {
+            const int wk = wf + k;
+            return a.part + ((size_t)wk * 2 + (k == 0 ? 1 : 0)) * SLOT;
+          };
+          if (a.mode == kModeStream) {
+            combine_pieces<D, GT>(piece, np, lane, hcnt,
+                                  a.out + ((size_t)cb * a.H + hbase) * D, nullptr, a.status);
+          } else {
+            combine_pieces<D, GT>(piece, np, lane, hcnt, nullptr,
+                                  a.part_out + (size_t)segid * SLOT, a.status);
+          }
+          if (lane == 0) a.counters[segid] = 0;
+        }
+      }
+    }
+
+    // Advance the consumer iterator.
+    if (++csp == cpg) {
+      csp = 0;
+      if (++cseg == SEGS) {
+        cseg = 0;
+        if (j + 1 < n) {
+          do { ++cb; } while (pages_of(cb) == 0);
+        }
+      }
+      if (j + 1 < n) cpg = pages_of(cb);
+    }
+  }
+
+  if (jfail >= 0) {
+    // Let copies still in flight land before the CTA's shared memory is released.
+    for (int j = jfail; j < issued; ++j) {
+      (void)mbar_wait_bounded(&wbar[j % DEPTH], (uint32_t)(j / DEPTH) & 1u, nullptr);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// LSE reduce: one warp per (sequence, kv-head, head tile) segment.
+// ---------------------------------------------------------------------------------------
+template <int D, int GT>
+__global__ void __launch_bounds__(128) reduce_kernel(const ReduceArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int SEGS = a.KVH * a.HT;
+  const int segid = blockIdx.x * 4 + warp;
+  if (segid >= a.B * SEGS) return;
+  const int b = segid / SEGS;
+  const int seg = segid - b * SEGS;
+  const int kvh = seg / a.HT;
+  const int ht = seg - kvh * a.HT;
+  const int hbase = kvh * a.G + ht * GT;
+  const int hcnt = min(GT, a.G - ht * GT);
+  int np = a.num_parts;
+  if (np <= 0) {
+    int c = __ldg(a.context_lens + b);
+    const int cap = a.max_blocks * a.bs;
+    c = c < 0 ? 0 : (c > cap ? cap : c);
+    const int pages = (c + kSubTokens - 1) / kSubTokens;
+    np = (pages + kSplitPages - 1) / kSplitPages;
+  }
+  __half* orow = a.out + ((size_t)b * a.H + hbase) * D;
+  if (np == 0) {
+    for (int i = lane; i < hcnt * D; i += 32) orow[(i / D) * D + (i % D)] = __float2half_rn(0.f);
+    if (lane == 0 && seg == 0) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
+    return;
+  }
+  const float* base = a.part + (size_t)segid * a.seg_stride;
+  combine_pieces<D, GT>([&](int k) { return base + (size_t)k * a.piece_stride; }, np, lane,
+                        hcnt, orow, nullptr, a.status);
+}
+
+// Tuned shapes: INT8 stages are 4.2 KB, FP16 stages 8 KB.
+constexpr int kWarpsI8 = 8, kDepthI8 = 4;
+constexpr int kWarpsF16 = 8, kDepthF16 = 3;
+
+template <int KVK, int GT>
+cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
+                       cudaStream_t stream) {
+  constexpr int W = KVK ? kWarpsI8 : kWarpsF16;
+  constexpr int DP = KVK ? kDepthI8 : kDepthF16;
+  using C = Tile<KVK, 128, GT, DP, W>;
+  auto kern = decode_kernel<KVK, 128, GT, DP, W>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)C::SMEM);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, W * 32, C::SMEM, stream>>>(a, maps[0], maps[1], maps[2], maps[3]);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int decode_warps_per_cta(int kv_i8) { return kv_i8 ? kWarpsI8 : kWarpsF16; }
+
+size_t decode_smem_bytes(int kv_i8, int gt) {
+  if (kv_i8) {
+    return gt == 8 ? Tile<1, 128, 8, kDepthI8, kWarpsI8>::SMEM
+                   : Tile<1, 128, 16, kDepthI8, kWarpsI8>::SMEM;
+  }
+  return gt == 8 ? Tile<0, 128, 8, kDepthF16, kWarpsF16>::SMEM
+                 : Tile<0, 128, 16, kDepthF16, kWarpsF16>::SMEM;
+}
+
+cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensorMap* maps,
+                          int grid, cudaStream_t stream) {
+  if (kv_i8) {
+    return gt == 8 ? launch_one<1, 8>(a, maps, grid, stream)
+                   : launch_one<1, 16>(a, maps, grid, stream);
+  }
+  return gt == 8 ? launch_one<0, 8>(a, maps, grid, stream)
+                 : launch_one<0, 16>(a, maps, grid, stream);
+}
+
+cudaError_t launch_reduce(int gt, const ReduceArgs& a, cudaStream_t stream) {
+  const int segs = a.B * a.KVH * a.HT;
+  const int grid = (segs + 3) / 4;
+  if (grid == 0) return cudaSuccess;
+  if (gt == 8) {
+    reduce_kernel<128, 8><<<grid, 128, 0, stream>>>(a);
+  } else {
+    reduce_kernel<128, 16><<<grid, 128, 0, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pa

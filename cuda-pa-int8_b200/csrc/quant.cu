@@ -1,0 +1,401 @@
+// Cache-write kernels for B200: per-token symmetric INT8 quantize-into-cache, FP16
+// copy-into-cache, block-granular prefill scatter, and the per-tensor absmax scale.
+//
+// Quantisation is bit-exact with the reference quantizer quantize_per_token
+// (tests/paged_decode_attn.py:106-112):
+//   amax  = max_d |x_d|                     (exact in the input dtype)
+//   amax' = max(amax, T(1e-8))              (T = input dtype; T(1e-8) is 0 for fp16)
+//   scale = float(T(float(amax') / 127))    (IEEE fp32 divide, round-to-nearest-even into T)
+//   q_d   = clamp(rint(float(x_d) / scale), -127, 127)   (IEEE divide, half-to-even)
+// A zero scale (all-zero or tiny fp16 rows) gives x/0 = +-inf -> +-127 and 0/0 = NaN -> 0,
+// which is what the reference produces on the CPU. These kernels are built without fast-math
+// so the divides stay IEEE (__fdiv_rn is used explicitly as well).
+
+#include "pa_common.cuh"
+#include "pa_internal.h"
+
+namespace pa {
+namespace {
+
+template <typename T> struct In;
+template <> struct In<__half> {
+  static __device__ __forceinline__ float ld(const __half* p) { return __half2float(*p); }
+  static __device__ __forceinline__ float clamp_floor() { return 0.f; }  // half(1e-8) == 0
+  static __device__ __forceinline__ float round_t(float v) {
+    return __half2float(__float2half_rn(v));
+  }
+};
+template <> struct In<__nv_bfloat16> {
+  static __device__ __forceinline__ float ld(const __nv_bfloat16* p) {
+    return __bfloat162float(*p);
+  }
+  static __device__ __forceinline__ float clamp_floor() {
+    return __bfloat162float(__float2bfloat16_rn(1e-8f));
+  }
+  static __device__ __forceinline__ float round_t(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+};
+template <> struct In<float> {
+  static __device__ __forceinline__ float ld(const float* p) { return *p; }
+  static __device__ __forceinline__ float clamp_floor() { return 1e-8f; }
+  static __device__ __forceinline__ float round_t(float v) { return v; }
+};
+
+// Per-token scale from the row absmax (quantize_per_token, tests/paged_decode_attn.py:109-110).
+template <typename T>
+__device__ __forceinline__ float token_scale(float amax) {
+  return In<T>::round_t(__fdiv_rn(fmaxf(amax, In<T>::clamp_floor()), 127.f));
+}
+
+__device__ __forceinline__ int8_t quant1(float x, float s) {
+  int q = __float2int_rn(__fdiv_rn(x, s));
+  q = q < -127 ? -127 : (q > 127 ? 127 : q);
+  return (int8_t)q;
+}
+
+// Load DPL consecutive input values starting at src (src aligned to DPL elements).
+template <typename T, int DPL>
+__device__ __forceinline__ void load_vals(const T* src, float (&x)[DPL]) {
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) x[e] = In<T>::ld(src + e);
+}
+
+// ---------------------------------------------------------------------------------------
+// Token-granular write: one warp per (token, kv-head, K|V) row.
+// ---------------------------------------------------------------------------------------
+template <typename T, bool I8, int D>
+__global__ void __launch_bounds__(256) write_rows_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
+    const int* __restrict__ slot_mapping, int N, int KVH, void* __restrict__ k_cache,
+    void* __restrict__ v_cache, float* __restrict__ k_scales, float* __restrict__ v_scales,
+    int NB, int bs, const float* __restrict__ kfix, const float* __restrict__ vfix,
+    int* status) {
+  constexpr int DPL = D / 32;
+  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long long)N * KVH * 2) return;
+  const int which = (int)(gw & 1);  // 0: K, 1: V
+  const long long row = gw >> 1;
+  const int n = (int)(row / KVH);
+  const int kvh = (int)(row - (long long)n * KVH);
+  const int slot = __ldg(slot_mapping + n);
+  if (slot < 0) return;  // padding token
+  const int blk = slot / bs;
+  const int off = slot - blk * bs;
+  if (blk >= NB) {
+    if (lane == 0) flag_error(status, PA_ERR_SLOT);
+    return;
+  }
+  const T* src = (which ? v : k) + (size_t)n * token_stride + (size_t)kvh * D + lane * DPL;
+  float x[DPL];
+  load_vals<T, DPL>(src, x);
+  const size_t page = (size_t)blk * KVH + kvh;
+  const int d0 = lane * DPL;
+
+  if constexpr (I8) {
+    float s;
+    const float* fix = which ? vfix : kfix;
+    if (fix != nullptr) {
+      s = __ldg(fix);
+    } else {
+      float am = 0.f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) am = fmaxf(am, fabsf(x[e]));
+      am = warp_max(am);
+      s = token_scale<T>(am);
+    }
+    int8_t qv[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) qv[e] = quant1(x[e], s);
+    int8_t* kc = reinterpret_cast<int8_t*>(k_cache);
+    int8_t* vc = reinterpret_cast<int8_t*>(v_cache);
+    if (which == 0) {
+      // K [.., D/8, bs, 8]: DPL (<= 8) consecutive d inside one 8-wide chunk.
+      int8_t* dst = kc + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
+      if constexpr (DPL == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(qv);
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) dst[e] = qv[e];
+      }
+      if (lane == 0) k_scales[page * bs + off] = s;
+    } else {
+      // V [.., D, bs]: one byte per head_dim row.
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) vc[(page * D + d0 + e) * bs + off] = qv[e];
+      if (lane == 0) v_scales[page * bs + off] = s;
+    }
+  } else {
+    __half hv[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) hv[e] = __float2half_rn(x[e]);
+    __half* kc = reinterpret_cast<__half*>(k_cache);
+    __half* vc = reinterpret_cast<__half*>(v_cache);
+    if (which == 0) {
+      __half* dst = kc + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
+      if constexpr (DPL == 4) {
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(hv);
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) dst[e] = hv[e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) vc[(page * D + d0 + e) * bs + off] = hv[e];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Block-granular prefill: one CTA per (block j, kv-head, sequence). Quantises (or rounds)
+// the block's tokens into shared memory, then writes the K page, the V page and the scales
+// with 16-byte stores. Tokens past the context are written as zeros with scale 0.
+// ---------------------------------------------------------------------------------------
+template <typename T, bool I8, int D>
+__global__ void __launch_bounds__(128) prefill_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, int L, int KVH,
+    const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
+    void* __restrict__ k_cache, void* __restrict__ v_cache, float* __restrict__ k_scales,
+    float* __restrict__ v_scales, int NB, int bs, const float* __restrict__ kfix,
+    const float* __restrict__ vfix, int* status) {
+  using OutT = typename std::conditional<I8, int8_t, __half>::type;
+  constexpr int DPL = D / 32;
+  constexpr int ELEM = sizeof(OutT);
+  extern __shared__ __align__(16) uint8_t sm[];
+  OutT* q_sm = reinterpret_cast<OutT*>(sm);                     // [bs][D]
+  float* s_sm = reinterpret_cast<float*>(sm + (size_t)bs * D * ELEM);  // [bs]
+
+  const int j = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int b = blockIdx.z;
+  int ctx = __ldg(context_lens + b);
+  const int cap = min(L, max_blocks * bs);
+  if (ctx > cap) {
+    if (threadIdx.x == 0 && j == 0 && kvh == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
+    ctx = cap;
+  }
+  if (ctx < 0) ctx = 0;
+  const int nblk = (ctx + bs - 1) / bs;
+  if (j >= nblk) return;
+  const int blk = __ldg(block_table + (size_t)b * max_blocks + j);
+  if (blk < 0 || blk >= NB) {
+    if (threadIdx.x == 0) flag_error(status, PA_ERR_BLOCK_ID);
+    return;
+  }
+  const int t0 = j * bs;
+  const int valid = min(bs, ctx - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t page = (size_t)blk * KVH + kvh;
+
+  for (int which = 0; which < 2; ++which) {
+    const T* src = which ? v : k;
+    const float* fix = which ? vfix : kfix;
+    for (int i = warp; i < bs; i += 4) {
+      float x[DPL];
+      if (i < valid) {
+        load_vals<T, DPL>(src + (((size_t)b * L + t0 + i) * KVH + kvh) * D + lane * DPL, x);
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) x[e] = 0.f;
+      }
+      if constexpr (I8) {
+        float s;
+        if (i >= valid) {
+          s = 0.f;
+        } else if (fix != nullptr) {
+          s = __ldg(fix);
+        } else {
+          float am = 0.f;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) am = fmaxf(am, fabsf(x[e]));
+          am = warp_max(am);
+          s = token_scale<T>(am);
+        }
+#pragma unroll
+        for (int e = 0; e < DPL; ++e)
+          q_sm[i * D + lane * DPL + e] = (i < valid) ? quant1(x[e], s) : (int8_t)0;
+        if (lane == 0) s_sm[i] = s;
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) q_sm[i * D + lane * DPL + e] = __float2half_rn(x[e]);
+      }
+    }
+    __syncthreads();
+    OutT* cache = reinterpret_cast<OutT*>(which ? v_cache : k_cache);
+    OutT* pg = cache + page * (size_t)D * bs;
+    constexpr int PER16 = 16 / ELEM;  // elements per 16-byte store
+    const int units = D * bs / PER16;
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      alignas(16) OutT tmp[PER16];
+      const int e0 = u * PER16;  // element offset inside the page
+      if (which == 0) {
+        // K page [D/8][bs][8]: element e0 -> chunk c, token t, lane-in-chunk w
+#pragma unroll
+        for (int e = 0; e < PER16; ++e) {
+          const int el = e0 + e;
+          const int c = el / (bs * 8);
+          const int rem = el - c * bs * 8;
+          const int t = rem >> 3;
+          const int w = rem & 7;
+          tmp[e] = q_sm[t * D + c * 8 + w];
+        }
+      } else {
+        // V page [D][bs]
+#pragma unroll
+        for (int e = 0; e < PER16; ++e) {
+          const int el = e0 + e;
+          const int d = el / bs;
+          const int t = el - d * bs;
+          tmp[e] = q_sm[t * D + d];
+        }
+      }
+      *reinterpret_cast<uint4*>(pg + e0) = *reinterpret_cast<const uint4*>(tmp);
+    }
+    if constexpr (I8) {
+      float* sc = (which ? v_scales : k_scales) + page * bs;
+      for (int t = threadIdx.x; t < bs; t += blockDim.x) sc[t] = s_sm[t];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Per-tensor absmax -> scale.
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void absmax_kernel(const T* __restrict__ x, long long n, unsigned int* out) {
+  float m = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float a = fabsf(In<T>::ld(x + i));
+    m = (a > m || a != a) ? a : m;  // keep NaN
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+template <typename T>
+__global__ void scale_finalize_kernel(const unsigned int* amax_bits, float* scale_out,
+                                      int semantics) {
+  const float amax = __uint_as_float(*amax_bits);
+  float s;
+  if (semantics == PA_SCALE_CLAMP_THEN_DIVIDE) {
+    s = token_scale<T>(amax);
+  } else {
+    s = fmaxf(In<T>::round_t(__fdiv_rn(amax, 127.f)), 1e-8f);
+  }
+  *scale_out = s;
+}
+
+template <typename T>
+cudaError_t launch_rows_t(bool i8, int D, const void* k, const void* v, long long ts,
+                          const int* slots, int N, int KVH, void* kc, void* vc, float* ks,
+                          float* vs, int NB, int bs, const float* kf, const float* vf,
+                          int* status, cudaStream_t st) {
+  const long long warps = (long long)N * KVH * 2;
+  const int grid = (int)((warps + 7) / 8);
+  if (grid == 0) return cudaSuccess;
+  const T* kk = static_cast<const T*>(k);
+  const T* vv = static_cast<const T*>(v);
+  if (D != 128) return cudaErrorInvalidValue;
+  if (i8) {
+    write_rows_kernel<T, true, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc, ks,
+                                                          vs, NB, bs, kf, vf, status);
+  } else {
+    write_rows_kernel<T, false, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
+                                                           ks, vs, NB, bs, kf, vf, status);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_prefill_t(bool i8, const void* k, const void* v, int S, int L, int KVH,
+                             const int* bt, const int* cl, int max_blocks, void* kc, void* vc,
+                             float* ks, float* vs, int NB, int bs, const float* kf,
+                             const float* vf, int* status, cudaStream_t st) {
+  if (S == 0 || max_blocks == 0) return cudaSuccess;
+  const dim3 grid(max_blocks, KVH, S);
+  const T* kk = static_cast<const T*>(k);
+  const T* vv = static_cast<const T*>(v);
+  if (i8) {
+    const size_t smem = (size_t)bs * 128 + bs * 4;
+    prefill_kernel<T, true, 128><<<grid, 128, smem, st>>>(kk, vv, L, KVH, bt, cl, max_blocks, kc,
+                                                          vc, ks, vs, NB, bs, kf, vf, status);
+  } else {
+    const size_t smem = (size_t)bs * 128 * 2 + bs * 4;
+    prefill_kernel<T, false, 128><<<grid, 128, smem, st>>>(kk, vv, L, KVH, bt, cl, max_blocks,
+                                                           kc, vc, ks, vs, NB, bs, kf, vf,
+                                                           status);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_write_rows(int in_dtype, bool i8, int D, const void* k, const void* v,
+                              long long ts, const int* slots, int N, int KVH, void* kc,
+                              void* vc, float* ks, float* vs, int NB, int bs, const float* kf,
+                              const float* vf, int* status, cudaStream_t st) {
+  switch (in_dtype) {
+    case PA_DTYPE_F16:
+      return launch_rows_t<__half>(i8, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
+                                   vf, status, st);
+    case PA_DTYPE_BF16:
+      return launch_rows_t<__nv_bfloat16>(i8, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB,
+                                          bs, kf, vf, status, st);
+    case PA_DTYPE_F32:
+      return launch_rows_t<float>(i8, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
+                                  vf, status, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_prefill(int in_dtype, bool i8, const void* k, const void* v, int S, int L,
+                           int KVH, const int* bt, const int* cl, int max_blocks, void* kc,
+                           void* vc, float* ks, float* vs, int NB, int bs, const float* kf,
+                           const float* vf, int* status, cudaStream_t st) {
+  switch (in_dtype) {
+    case PA_DTYPE_F16:
+      return launch_prefill_t<__half>(i8, k, v, S, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs,
+                                      NB, bs, kf, vf, status, st);
+    case PA_DTYPE_BF16:
+      return launch_prefill_t<__nv_bfloat16>(i8, k, v, S, L, KVH, bt, cl, max_blocks, kc, vc,
+                                             ks, vs, NB, bs, kf, vf, status, st);
+    case PA_DTYPE_F32:
+      return launch_prefill_t<float>(i8, k, v, S, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs,
+                                     NB, bs, kf, vf, status, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float* scale_out,
+                                int semantics, unsigned int* scratch, int num_sms,
+                                cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(unsigned int), st);
+  if (e != cudaSuccess) return e;
+  const int grid = num_sms * 4;
+  switch (in_dtype) {
+    case PA_DTYPE_F16:
+      if (n > 0) absmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), n, scratch);
+      scale_finalize_kernel<__half><<<1, 1, 0, st>>>(scratch, scale_out, semantics);
+      break;
+    case PA_DTYPE_BF16:
+      if (n > 0)
+        absmax_kernel<__nv_bfloat16>
+            <<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, scratch);
+      scale_finalize_kernel<__nv_bfloat16><<<1, 1, 0, st>>>(scratch, scale_out, semantics);
+      break;
+    case PA_DTYPE_F32:
+      if (n > 0) absmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), n, scratch);
+      scale_finalize_kernel<float><<<1, 1, 0, st>>>(scratch, scale_out, semantics);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pa

@@ -1,0 +1,369 @@
+"""Torch-facing wrappers of the C ABI.
+
+Each op checks its arguments with the error conditions of the reference launchers
+(kernels/paged_attention_v4_splitk.cu:197-205, kernels/paged_attention_v6_splitk_int8.cu:
+201-221 and siblings) and raises RuntimeError like their TORCH_CHECKs, then calls the
+library on the current CUDA stream of the tensors' device. Temporaries (split partials,
+arrival counters, the device status word) live in a per-(device, stream) workspace that is
+zero-filled once when allocated and kept for later calls.
+"""
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+HEAD_DIM = 128
+X = 8
+
+_DTYPE_CODE = {
+    torch.float16: _lib.PA_DTYPE_F16,
+    torch.bfloat16: _lib.PA_DTYPE_BF16,
+    torch.float32: _lib.PA_DTYPE_F32,
+}
+
+_workspaces = {}
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(device, nbytes):
+    """The zero-initialised workspace of (device, current stream), grown to nbytes."""
+    stream = _stream(device)
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    nbytes = max(int(nbytes), 256)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def read_status(device=None):
+    """OR of the device status words of this device's workspaces, which are then cleared
+    (synchronises). Bits are the PA_ERR_* codes of include/pa_b200.h."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    status = 0
+    for (idx, stream), ws in list(_workspaces.items()):
+        if idx != device.index:
+            continue
+        out = ctypes.c_int(0)
+        _lib.check(_lib.lib().pa_read_status(ws.data_ptr(), ctypes.byref(out), stream),
+                   "pa_read_status")
+        status |= out.value
+    return status
+
+
+def check_status(device=None):
+    """Raise RuntimeError if a kernel on `device` recorded an error since the last check."""
+    status = read_status(device)
+    if status:
+        raise RuntimeError("paged-attention kernel reported: " +
+                           _lib.lib().pa_status_string(status).decode() + f" (status {status})")
+
+
+class _Guard:
+    """Make `device` current for the duration of a call (no-op when it already is)."""
+
+    def __init__(self, device):
+        self.device = device
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.device.index:
+            self.prev = cur
+            torch.cuda.set_device(self.device)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+def _require(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
+                       int8, k_scales, v_scales, validate, out_required=True):
+    _require(q.is_cuda and (out is None or out.is_cuda), "tensors must be on CUDA")
+    _require(q.dtype == torch.float16, "q must be fp16")
+    if int8:
+        _require(k_cache.dtype == torch.int8, "k_cache must be int8")
+        _require(v_cache.dtype == torch.int8, "v_cache must be int8")
+        _require(k_scales is not None and k_scales.dtype == torch.float32,
+                 "k_scales must be fp32")
+        _require(v_scales is not None and v_scales.dtype == torch.float32,
+                 "v_scales must be fp32")
+    else:
+        _require(k_cache.dtype == torch.float16, "k_cache must be fp16")
+        _require(v_cache.dtype == torch.float16, "v_cache must be fp16")
+    _require(block_table.dtype == torch.int32, "block_table must be int32")
+    _require(context_lens.dtype == torch.int32, "context_lens must be int32")
+    dev = q.device
+    tensors = [k_cache, v_cache, block_table, context_lens] + ([out] if out is not None else [])
+    if int8:
+        tensors += [k_scales, v_scales]
+    for t in tensors:
+        _require(t.device == dev, "all tensors must be on the same CUDA device")
+        _require(t.is_contiguous(), "all tensors must be contiguous")
+    _require(q.dim() == 3, "q must be [num_seqs, num_heads, head_dim]")
+    B, H, D = q.shape
+    if out is not None:
+        _require(tuple(out.shape) == (B, H, D) and out.dtype == torch.float16,
+                 "out must be fp16 with the shape of q")
+    _require(k_cache.dim() == 5, "k_cache must be [num_blocks, kv_heads, head_dim/x, block_size, x]")
+    NB, KVH, DX, BS, x = k_cache.shape
+    if int8:
+        _require(x == 8, "int8 K cache requires x == 8")
+    _require(x == X, "K cache requires x == 8")
+    _require(D == HEAD_DIM, f"head_dim {D} unsupported (this build: {HEAD_DIM})")
+    _require(DX * x == D, "k_cache head_dim/x does not match q")
+    _require(block_size % 16 == 0 and 128 % block_size == 0,
+             "block_size must divide TILE (multiple of 16)")
+    _require(BS == block_size, f"k_cache block dimension {BS} != block_size {block_size}")
+    _require(tuple(v_cache.shape) == (NB, KVH, D, block_size),
+             "v_cache must be [num_blocks, kv_heads, head_dim, block_size]")
+    if int8:
+        _require(tuple(k_scales.shape) == (NB, KVH, block_size) and
+                 tuple(v_scales.shape) == (NB, KVH, block_size),
+                 "scales must be [num_blocks, kv_heads, block_size]")
+    _require(KVH > 0 and H % KVH == 0, "num_heads must be a multiple of num_kv_heads")
+    _require(block_table.dim() == 2 and block_table.shape[0] == B,
+             "block_table must be [num_seqs, max_blocks_per_seq]")
+    _require(context_lens.dim() == 1 and context_lens.shape[0] == B,
+             "context_lens must be [num_seqs]")
+    if validate and B > 0:
+        mm = torch.stack([context_lens.min(), context_lens.max()]).cpu()
+        _require(int(mm[0]) >= 1, "context_lens must be >= 1 (empty sequences unsupported)")
+        _require(int(mm[1]) <= block_table.shape[1] * block_size,
+                 "context_lens exceeds max_blocks_per_seq * block_size")
+    return B, H, KVH, D, NB
+
+
+def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
+           k_scales=None, v_scales=None, splitk=False, validate=True):
+    """Paged decode attention into `out` (fp16 [num_seqs, num_heads, head_dim]).
+
+    FP16 cache when k_scales is None, otherwise INT8 with per-token fp32 scales. splitk
+    selects the partition + LSE-reduce kernel pair (512-token splits); otherwise the
+    single-pass kernel with the fused combine runs. validate=False skips the one host sync
+    that checks context_lens (the kernels still flag bad lengths in the status word).
+    """
+    int8 = k_scales is not None or k_cache.dtype == torch.int8
+    B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
+                                          block_size, int8, k_scales, v_scales, validate)
+    if B == 0:
+        return out
+    L = _lib.lib()
+    max_blocks = block_table.shape[1]
+    with _Guard(q.device):
+        kv = _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16
+        need = L.pa_decode_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv,
+                                           1 if splitk else 0)
+        _require(need > 0, "unsupported decode shape: " + _lib.last_error())
+        ws = workspace(q.device, need)
+        stream = _stream(q.device)
+        if int8:
+            fn = L.pa_splitk_i8 if splitk else L.pa_decode_i8
+            rc = fn(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                    k_scales.data_ptr(), v_scales.data_ptr(), block_table.data_ptr(),
+                    context_lens.data_ptr(), B, H, KVH, D, NB, block_size, max_blocks,
+                    float(scale), ws.data_ptr(), ws.numel(), stream)
+        else:
+            fn = L.pa_splitk_f16 if splitk else L.pa_decode_f16
+            rc = fn(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                    block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D, NB,
+                    block_size, max_blocks, float(scale), ws.data_ptr(), ws.numel(), stream)
+        _lib.check(rc, "paged decode")
+    return out
+
+
+def partial_floats(num_heads, num_kv_heads, head_dim=HEAD_DIM):
+    return _lib.lib().pa_partial_floats(num_heads, num_kv_heads, head_dim)
+
+
+def decode_partial(q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
+                   k_scales=None, v_scales=None, partials=None):
+    """Un-normalised per-(sequence, kv-head) partials (O, m, l) for this device's token
+    ranges: fp32 [num_seqs, num_kv_heads * slot]. Sequences with context 0 give empty
+    partials. Used to split one sequence's context across GPUs."""
+    int8 = k_scales is not None or k_cache.dtype == torch.int8
+    B, H, KVH, D, NB = _check_decode_args(None, q, k_cache, v_cache, block_table, context_lens,
+                                          block_size, int8, k_scales, v_scales, validate=False)
+    per = partial_floats(H, KVH, D) // KVH * KVH
+    if partials is None:
+        partials = torch.empty(B, per, dtype=torch.float32, device=q.device)
+    _require(partials.dtype == torch.float32 and partials.is_contiguous() and
+             partials.numel() == B * per, "partials must be fp32 [num_seqs, per_seq_floats]")
+    if B == 0:
+        return partials
+    L = _lib.lib()
+    max_blocks = block_table.shape[1]
+    with _Guard(q.device):
+        kv = _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16
+        need = L.pa_decode_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv, 0)
+        _require(need > 0, "unsupported decode shape: " + _lib.last_error())
+        ws = workspace(q.device, need)
+        rc = L.pa_decode_partial(kv, partials.data_ptr(), q.data_ptr(), k_cache.data_ptr(),
+                                 v_cache.data_ptr(), _ptr(k_scales), _ptr(v_scales),
+                                 block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D,
+                                 NB, block_size, max_blocks, float(scale), ws.data_ptr(),
+                                 ws.numel(), _stream(q.device))
+        _lib.check(rc, "partial decode")
+    return partials
+
+
+def merge_partials(out, partials, num_heads, num_kv_heads):
+    """LSE-merge partials gathered from several GPUs, fp32 [num_parts, num_seqs, ...], into
+    out fp16 [num_seqs, num_heads, head_dim]."""
+    _require(out.is_cuda and partials.is_cuda, "tensors must be on CUDA")
+    _require(partials.dtype == torch.float32 and partials.is_contiguous(),
+             "partials must be contiguous fp32")
+    P, B = partials.shape[0], partials.shape[1]
+    _require(tuple(out.shape) == (B, num_heads, HEAD_DIM) and out.dtype == torch.float16,
+             "out must be fp16 [num_seqs, num_heads, head_dim]")
+    with _Guard(out.device):
+        ws = workspace(out.device, 256)
+        rc = _lib.lib().pa_merge_partials(out.data_ptr(), partials.data_ptr(), P, B, num_heads,
+                                          num_kv_heads, HEAD_DIM, ws.data_ptr(),
+                                          _stream(out.device))
+        _lib.check(rc, "merge partials")
+    return out
+
+
+# ---------------------------------------------------------------------------------------
+# Cache writes
+# ---------------------------------------------------------------------------------------
+def _check_rows(key, value):
+    _require(key.is_cuda and value.is_cuda, "tensors must be on CUDA")
+    _require(key.dtype in _DTYPE_CODE and value.dtype == key.dtype,
+             "key/value must both be fp16, bf16 or fp32")
+    _require(key.dim() == 3 and key.shape == value.shape,
+             "key/value must be [num_tokens, num_kv_heads, head_dim]")
+    _require(key.stride(2) == 1 and key.stride(1) == key.shape[2] and
+             value.stride() == key.stride(), "key/value rows must be contiguous")
+
+
+def quantize_into_cache(key, value, k_cache, v_cache, k_scales, v_scales, slot_mapping,
+                        block_size=16, *, k_scale=None, v_scale=None):
+    """Per-token symmetric INT8 write of key/value [num_tokens, kv_heads, head_dim] into the
+    paged cache at slot_mapping (int32, block*block_size+offset; negative = skip).
+
+    Values and scales are bit-identical to quantize_per_token
+    (tests/paged_decode_attn.py:106-112). With k_scale/v_scale (one fp32 device scalar each)
+    the given per-tensor scale is used instead, as PagedKVCache.decode_append does in
+    per-tensor mode (benchmarks/int8_bridge/paged_cache.py:142-145).
+    """
+    _check_rows(key, value)
+    _require(k_cache.dtype == torch.int8 and v_cache.dtype == torch.int8, "cache must be int8")
+    _require(k_scales.dtype == torch.float32 and v_scales.dtype == torch.float32,
+             "scales must be fp32")
+    _require(slot_mapping.dtype == torch.int32 and slot_mapping.is_cuda,
+             "slot_mapping must be int32 on CUDA")
+    N, KVH, D = key.shape
+    _require(slot_mapping.numel() == N, "slot_mapping must have one entry per token")
+    _require(k_cache.shape[1] == KVH and k_cache.shape[3] == block_size,
+             "cache kv_heads/block_size mismatch")
+    for t in (k_cache, v_cache, k_scales, v_scales, slot_mapping):
+        _require(t.is_contiguous() and t.device == key.device,
+                 "cache tensors must be contiguous and on the key's device")
+    for t in (k_scale, v_scale):
+        if t is not None:
+            _require(t.dtype == torch.float32 and t.numel() == 1 and t.device == key.device,
+                     "fixed scales must be one fp32 element on the key's device")
+    with _Guard(key.device):
+        ws = workspace(key.device, 256)
+        rc = _lib.lib().pa_quantize_into_cache(
+            key.data_ptr(), value.data_ptr(), _DTYPE_CODE[key.dtype], key.stride(0),
+            slot_mapping.data_ptr(), N, KVH, D, k_cache.data_ptr(), v_cache.data_ptr(),
+            k_scales.data_ptr(), v_scales.data_ptr(), k_cache.shape[0], block_size,
+            _ptr(k_scale), _ptr(v_scale), ws.data_ptr(), _stream(key.device))
+        _lib.check(rc, "quantize_into_cache")
+
+
+def write_into_cache(key, value, k_cache, v_cache, slot_mapping, block_size=16):
+    """FP16 copy of key/value [num_tokens, kv_heads, head_dim] into an fp16 paged cache."""
+    _check_rows(key, value)
+    _require(k_cache.dtype == torch.float16 and v_cache.dtype == torch.float16,
+             "cache must be fp16")
+    _require(slot_mapping.dtype == torch.int32 and slot_mapping.is_cuda,
+             "slot_mapping must be int32 on CUDA")
+    N, KVH, D = key.shape
+    _require(slot_mapping.numel() == N, "slot_mapping must have one entry per token")
+    _require(k_cache.shape[1] == KVH and k_cache.shape[3] == block_size,
+             "cache kv_heads/block_size mismatch")
+    for t in (k_cache, v_cache, slot_mapping):
+        _require(t.is_contiguous() and t.device == key.device,
+                 "cache tensors must be contiguous and on the key's device")
+    with _Guard(key.device):
+        ws = workspace(key.device, 256)
+        rc = _lib.lib().pa_write_into_cache_f16(
+            key.data_ptr(), value.data_ptr(), _DTYPE_CODE[key.dtype], key.stride(0),
+            slot_mapping.data_ptr(), N, KVH, D, k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.shape[0], block_size, ws.data_ptr(), _stream(key.device))
+        _lib.check(rc, "write_into_cache")
+
+
+def prefill_into_cache(k, v, k_cache, v_cache, block_table, context_lens, block_size=16, *,
+                       k_scales=None, v_scales=None, k_scale=None, v_scale=None):
+    """Bulk write of contiguous per-sequence K/V [num_seqs, max_len, kv_heads, head_dim] into
+    the blocks listed by block_table (one CTA per block, full-page 16-byte stores). INT8
+    caches are quantised per token (or with k_scale/v_scale); FP16 caches get a copy.
+    Tokens past a sequence's context inside its last block are written as zeros."""
+    _require(k.is_cuda and v.is_cuda, "tensors must be on CUDA")
+    _require(k.dtype in _DTYPE_CODE and v.dtype == k.dtype, "k/v must be fp16, bf16 or fp32")
+    _require(k.dim() == 4 and k.shape == v.shape and k.is_contiguous() and v.is_contiguous(),
+             "k/v must be contiguous [num_seqs, max_len, kv_heads, head_dim]")
+    S, Lmax, KVH, D = k.shape
+    int8 = k_cache.dtype == torch.int8
+    _require(int8 or k_cache.dtype == torch.float16, "cache must be int8 or fp16")
+    _require(block_table.dtype == torch.int32 and context_lens.dtype == torch.int32,
+             "block_table and context_lens must be int32")
+    _require(block_table.dim() == 2 and block_table.shape[0] == S and context_lens.numel() == S,
+             "block_table must be [num_seqs, max_blocks] and context_lens [num_seqs]")
+    tensors = [k_cache, v_cache, block_table, context_lens]
+    if int8:
+        _require(k_scales is not None and v_scales is not None, "int8 cache needs scales")
+        tensors += [k_scales, v_scales]
+    for t in tensors:
+        _require(t.is_contiguous() and t.device == k.device,
+                 "cache tensors must be contiguous and on k's device")
+    with _Guard(k.device):
+        ws = workspace(k.device, 256)
+        rc = _lib.lib().pa_prefill_into_cache(
+            k.data_ptr(), v.data_ptr(), _DTYPE_CODE[k.dtype], S, Lmax, KVH, D,
+            block_table.data_ptr(), context_lens.data_ptr(), block_table.shape[1],
+            _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16, k_cache.data_ptr(),
+            v_cache.data_ptr(), _ptr(k_scales), _ptr(v_scales), k_cache.shape[0], block_size,
+            _ptr(k_scale), _ptr(v_scale), ws.data_ptr(), _stream(k.device))
+        _lib.check(rc, "prefill_into_cache")
+
+
+def absmax_scale(x, semantics=_lib.PA_SCALE_CLAMP_THEN_DIVIDE):
+    """Per-tensor INT8 scale of x as a 0-d fp32 device tensor.
+
+    CLAMP_THEN_DIVIDE matches quantize_per_tensor (tests/paged_decode_attn.py:118-119);
+    DIVIDE_THEN_CLAMP matches PagedKVCache.prefill's per-tensor scale
+    (benchmarks/int8_bridge/paged_cache.py:101-102)."""
+    _require(x.is_cuda and x.dtype in _DTYPE_CODE and x.is_contiguous(),
+             "x must be a contiguous fp16/bf16/fp32 CUDA tensor")
+    out = torch.empty((), dtype=torch.float32, device=x.device)
+    with _Guard(x.device):
+        scratch = torch.empty(1, dtype=torch.int32, device=x.device)
+        rc = _lib.lib().pa_absmax_scale(x.data_ptr(), _DTYPE_CODE[x.dtype], x.numel(),
+                                        out.data_ptr(), semantics, scratch.data_ptr(),
+                                        _stream(x.device))
+        _lib.check(rc, "absmax_scale")
+    return out

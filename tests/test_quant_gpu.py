@@ -1,0 +1,258 @@
+"""GPU parity of the cache-write kernels: bit-exact INT8 values and scales against the
+oracle (which the golden vectors pin to the reference quantizer), FP16 copies, the bulk
+prefill scatter, per-tensor scales and the bridge cache."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import gen
+import pa_oracle
+from pa_testlib import to_cuda
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _ops():
+    from pa_b200 import ops
+    return ops
+
+
+def _caches(nb, kvh, bs=16, int8=True):
+    dt = torch.int8 if int8 else torch.float16
+    kc = torch.zeros(nb, kvh, 16, bs, 8, dtype=dt, device="cuda")
+    vc = torch.zeros(nb, kvh, 128, bs, dtype=dt, device="cuda")
+    ks = torch.zeros(nb, kvh, bs, dtype=torch.float32, device="cuda")
+    vs = torch.zeros(nb, kvh, bs, dtype=torch.float32, device="cuda")
+    return kc, vc, ks, vs
+
+
+def _oracle_rows(k, v, slots, nb, kvh, bs, in_dtype, k_fix=None, v_fix=None):
+    """Oracle cache after writing rows k, v [N, KVH, D] at slots (negative skipped)."""
+    if k_fix is None:
+        kq, ksc = pa_oracle.quantize_per_token(k, in_dtype)
+        vq, vsc = pa_oracle.quantize_per_token(v, in_dtype)
+    else:
+        kq = pa_oracle.quantize_with_scale(k.astype(np.float32), k_fix)
+        vq = pa_oracle.quantize_with_scale(v.astype(np.float32), v_fix)
+        ksc = np.full(k.shape[:-1], k_fix, np.float32)
+        vsc = np.full(v.shape[:-1], v_fix, np.float32)
+    kc = np.zeros((nb, kvh, 16, bs, 8), np.int8)
+    vc = np.zeros((nb, kvh, 128, bs), np.int8)
+    ks = np.zeros((nb, kvh, bs), np.float32)
+    vs = np.zeros((nb, kvh, bs), np.float32)
+    for n, s in enumerate(slots):
+        if s < 0:
+            continue
+        b, o = s // bs, s % bs
+        kc[b, :, :, o, :] = kq[n].reshape(kvh, 16, 8)
+        vc[b, :, :, o] = vq[n]
+        ks[b, :, o] = ksc[n]
+        vs[b, :, o] = vsc[n]
+    return kc, vc, ks, vs
+
+
+def _bits_equal(a, b):
+    a = a.cpu().numpy() if hasattr(a, "cpu") else a
+    if a.dtype == np.float32:
+        return np.array_equal(a.view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+    return np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("source", ["golden16", "golden32", "goldenbf16", "outlier"])
+def test_quantize_rows_bit_exact(source):
+    gold = np.load(os.path.join(GOLD, "quant_rows.npz"))
+    if source == "golden16":
+        x, dtype, tdt = gold["x16"], "f16", torch.float16
+    elif source == "golden32":
+        x, dtype, tdt = gold["x32"], "f32", torch.float32
+    elif source == "goldenbf16":
+        x = (gold["xbf16_bits"].astype(np.uint32) << 16).view(np.float32)
+        dtype, tdt = "bf16", torch.bfloat16
+    else:
+        g = gen.Gen(3)
+        x = gen.kv_values(g, (300, 1, 128), "lognormal_outlier")[:, 0].astype(np.float16)
+        dtype, tdt = "f16", torch.float16
+    R = x.shape[0] - x.shape[0] % 2
+    x = x[:R]
+    kvh, bs = 2, 16
+    N = R // kvh
+    k = x.reshape(N, kvh, 128)
+    v = np.ascontiguousarray(k[::-1])
+    nb = (N + bs - 1) // bs + 3
+    slots = gen.Gen(4).permutation(nb * bs)[:N].astype(np.int32)
+    slots[1] = -1  # padding token: skipped
+    kc, vc, ks, vs = _caches(nb, kvh, bs)
+    tk = torch.from_numpy(np.ascontiguousarray(k)).to(tdt).cuda() if tdt == torch.bfloat16 \
+        else torch.from_numpy(np.ascontiguousarray(k)).cuda()
+    tv = torch.from_numpy(np.ascontiguousarray(v)).to(tdt).cuda() if tdt == torch.bfloat16 \
+        else torch.from_numpy(np.ascontiguousarray(v)).cuda()
+    _ops().quantize_into_cache(tk, tv, kc, vc, ks, vs, torch.from_numpy(slots).cuda(), bs)
+    okc, ovc, oks, ovs = _oracle_rows(k, v, slots, nb, kvh, bs, dtype)
+    assert _bits_equal(kc, okc) and _bits_equal(vc, ovc)
+    assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
+
+
+def test_quantize_matches_golden_directly():
+    """Kernel scales/values for the golden fp16 rows equal the reference's, element for
+    element (no oracle in between)."""
+    gold = np.load(os.path.join(GOLD, "quant_rows.npz"))
+    x = gold["x16"]
+    N = x.shape[0]
+    kc, vc, ks, vs = _caches(N, 1, 16)
+    slots = (np.arange(N, dtype=np.int32) * 16)  # token n -> block n, offset 0
+    tx = torch.from_numpy(x.reshape(N, 1, 128)).cuda()
+    _ops().quantize_into_cache(tx, tx, kc, vc, ks, vs, torch.from_numpy(slots).cuda(), 16)
+    got_q = kc[:, 0, :, 0, :].reshape(N, 128).cpu().numpy()
+    got_s = ks[:, 0, 0].cpu().numpy()
+    assert np.array_equal(got_q, gold["q16"])
+    assert np.array_equal(got_s.view(np.uint32), gold["s16"].view(np.uint32))
+    got_v = vc[:, 0, :, 0].cpu().numpy()
+    assert np.array_equal(got_v, gold["q16"])
+
+
+def test_quantize_fixed_scale():
+    g = gen.Gen(12)
+    k = gen.kv_values(g, (40, 2, 128), "lognormal_outlier").astype(np.float16)
+    v = gen.kv_values(g, (40, 2, 128), "normal").astype(np.float16)
+    sk, sv = np.float32(0.37), np.float32(0.021)
+    slots = np.arange(40, dtype=np.int32) + 5
+    kc, vc, ks, vs = _caches(4, 2)
+    tk, tv = to_cuda(k, v)
+    _ops().quantize_into_cache(tk, tv, kc, vc, ks, vs, torch.from_numpy(slots).cuda(), 16,
+                               k_scale=torch.tensor(sk, device="cuda"),
+                               v_scale=torch.tensor(sv, device="cuda"))
+    okc, ovc, oks, ovs = _oracle_rows(k, v, slots, 4, 2, 16, "f16", sk, sv)
+    assert _bits_equal(kc, okc) and _bits_equal(vc, ovc)
+    assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
+
+
+def test_out_of_range_slot_flagged():
+    ops = _ops()
+    ops.read_status()
+    k = torch.randn(3, 2, 128, dtype=torch.float16, device="cuda")
+    kc, vc, ks, vs = _caches(2, 2)
+    slots = torch.tensor([0, 999, 5], dtype=torch.int32, device="cuda")
+    ops.quantize_into_cache(k, k, kc, vc, ks, vs, slots, 16)
+    torch.cuda.synchronize()
+    assert ops.read_status() & 256  # PA_ERR_SLOT
+
+
+def test_fp16_write_into_cache():
+    g = gen.Gen(13)
+    k = gen.kv_values(g, (50, 4, 128), "normal")
+    v = gen.kv_values(g, (50, 4, 128), "normal")
+    slots = gen.Gen(14).permutation(64)[:50].astype(np.int32)
+    kc, vc, _, _ = _caches(4, 4, int8=False)
+    tk, tv = to_cuda(k, v)  # fp32 input: rounded to fp16 by the kernel
+    _ops().write_into_cache(tk, tv, kc, vc, torch.from_numpy(slots).cuda(), 16)
+    ok = np.zeros((4, 4, 16, 16, 8), np.float16)
+    ov = np.zeros((4, 4, 128, 16), np.float16)
+    for n, s in enumerate(slots):
+        ok[s // 16, :, :, s % 16, :] = k[n].astype(np.float16).reshape(4, 16, 8)
+        ov[s // 16, :, :, s % 16] = v[n].astype(np.float16)
+    assert np.array_equal(kc.cpu().numpy().view(np.uint16), ok.view(np.uint16))
+    assert np.array_equal(vc.cpu().numpy().view(np.uint16), ov.view(np.uint16))
+
+
+@pytest.mark.parametrize("bs", [16, 32, 64])
+@pytest.mark.parametrize("int8", [True, False])
+def test_prefill_scatter(bs, int8):
+    lens = [1, 33, 200, 64]
+    c = gen.decode_case(15, 4, 8, 2, lens, block_size=bs, dist="lognormal_outlier",
+                        num_blocks=40)
+    k, v, cl, bt, nb = c["k"], c["v"], c["context_lens"], c["block_table"], c["num_blocks"]
+    kc, vc, ks, vs = _caches(nb, 2, bs, int8)
+    tk, tv, tbt, tcl = to_cuda(k, v, bt, cl)
+    kw = dict(k_scales=ks, v_scales=vs) if int8 else {}
+    _ops().prefill_into_cache(tk, tv, kc, vc, tbt, tcl, bs, **kw)
+    if int8:
+        kq, ksc = pa_oracle.quantize_per_token(k, "f16")
+        vq, vsc = pa_oracle.quantize_per_token(v, "f16")
+        okc, ovc = pa_oracle.scatter_paged_cache(kq, vq, cl, bt, nb, bs)
+        oks = pa_oracle.scatter_scales(ksc, cl, bt, nb, 2, bs)
+        ovs = pa_oracle.scatter_scales(vsc, cl, bt, nb, 2, bs)
+        assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
+    else:
+        okc, ovc = pa_oracle.scatter_paged_cache(k, v, cl, bt, nb, bs)
+    assert np.array_equal(kc.cpu().numpy().view(np.uint8), okc.view(np.uint8))
+    assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
+def test_absmax_scales(dtype):
+    from pa_b200 import _lib
+    g = gen.Gen(16)
+    x = gen.kv_values(g, (33, 2, 128), "lognormal_outlier")
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dtype]
+    tx = torch.from_numpy(x).to(tdt).cuda()
+    xr = tx.float().cpu().numpy()
+    a = _ops().absmax_scale(tx, _lib.PA_SCALE_CLAMP_THEN_DIVIDE).item()
+    b = _ops().absmax_scale(tx, _lib.PA_SCALE_DIVIDE_THEN_CLAMP).item()
+    assert np.float32(a) == pa_oracle.quantize_per_tensor(xr, dtype)[1]
+    assert np.float32(b) == pa_oracle.bridge_tensor_scale(xr, dtype)
+    z = torch.zeros(10, 128, dtype=tdt, device="cuda")
+    assert np.float32(_ops().absmax_scale(z).item()) == pa_oracle.quantize_per_tensor(
+        np.zeros((10, 128), np.float32), dtype)[1]
+
+
+@pytest.mark.parametrize("variant", ["fp16", "int8_per_token", "int8_per_tensor"])
+def test_bridge_cache_matches_reference_golden(variant):
+    from pa_b200.paged_cache import PagedKVCache
+    gold = np.load(os.path.join(GOLD, "bridge_cache.npz"))
+    k, v = torch.from_numpy(gold["k"]).cuda(), torch.from_numpy(gold["v"]).cuda()
+    c = PagedKVCache(1, 2, 128, 40, variant=variant, device="cuda")
+    c.prefill(0, k[:-1], v[:-1])
+    assert c.decode_append(0, k[-1], v[-1]) == k.shape[0]
+    assert np.array_equal(c.k_cache[0].cpu().numpy().view(np.uint8),
+                          gold[f"{variant}_k"].view(np.uint8))
+    assert np.array_equal(c.v_cache[0].cpu().numpy().view(np.uint8),
+                          gold[f"{variant}_v"].view(np.uint8))
+    if variant != "fp16":
+        assert _bits_equal(c.k_scales[0], gold[f"{variant}_ks"])
+        assert _bits_equal(c.v_scales[0], gold[f"{variant}_vs"])
+
+
+@pytest.mark.parametrize("variant", ["fp16", "int8_per_token", "int8_per_tensor"])
+@pytest.mark.parametrize("clen", [17, 31, 128, 500])
+def test_bridge_decode_append_then_decode(variant, clen):
+    """The bridge flow of tests/test_int8_bridge.py:104-128 at Qwen's 12/2 heads: prefill
+    clen-1 tokens, append one, decode with the split-K op, compare with the oracle."""
+    from pa_b200 import cuda_ext
+    from pa_b200.paged_cache import PagedKVCache
+    from pa_testlib import assert_close, scale_for
+    g = gen.Gen(17)
+    k = gen.kv_values(g, (clen, 2, 128), "normal").astype(np.float16)
+    v = gen.kv_values(g, (clen, 2, 128), "normal").astype(np.float16)
+    q = g.normal((1, 12, 128)).astype(np.float16)
+    c = PagedKVCache(1, 2, 128, clen, variant=variant, device="cuda")
+    tk, tv, tq = to_cuda(k, v, q)
+    c.prefill(0, tk[:-1], tv[:-1])
+    assert c.decode_append(0, tk[-1], tv[-1]) == clen
+    out = torch.empty_like(tq)
+    ctx = c.context_lens(0)
+    if c.is_int8:
+        cuda_ext.VARIANTS_INT8["splitk_int8"](out, tq, c.k_cache[0], c.v_cache[0],
+                                              c.k_scales[0], c.v_scales[0], c.block_table, ctx,
+                                              scale_for(), 16)
+        kd, vd = pa_oracle.dequantize_kv(c.k_cache[0].cpu().numpy(), c.v_cache[0].cpu().numpy(),
+                                         c.k_scales[0].cpu().numpy(), c.v_scales[0].cpu().numpy())
+    else:
+        cuda_ext.VARIANTS["splitk"](out, tq, c.k_cache[0], c.v_cache[0], c.block_table, ctx,
+                                    scale_for(), 16)
+        kd, vd = c.k_cache[0].cpu().numpy(), c.v_cache[0].cpu().numpy()
+    ref = pa_oracle.paged_decode_attention(q, kd, vd, c.block_table.cpu().numpy(),
+                                           np.array([clen]))
+    assert_close(out, ref)
+
+
+def test_int8_cache_smaller_than_fp16():
+    from pa_b200.paged_cache import PagedKVCache
+    kw = dict(num_layers=28, num_kv_heads=2, head_dim=128, max_len=2048, device="cuda")
+    fp16 = PagedKVCache(variant="fp16", **kw).kv_bytes()
+    int8 = PagedKVCache(variant="int8_per_token", **kw).kv_bytes()
+    assert int8 / fp16 < 0.6
