@@ -50,8 +50,11 @@ struct Tile {
   static constexpr int ELEM = I8 ? 1 : 2;
   static constexpr int KT = D * kSubTokens * ELEM;  // K tile bytes
   static constexpr int VT = D * kSubTokens * ELEM;  // V tile bytes
-  static constexpr int ST = I8 ? 128 : 0;           // 16 K scales + 16 V scales
-  static constexpr uint32_t TX = KT + VT + ST;      // bytes per stage
+  // Scale tiles: 16 K scales at +0 and 16 V scales at +128 (tensor-copy destinations are
+  // kept 128-byte aligned); 128 bytes of them are transferred per stage.
+  static constexpr int ST = I8 ? 256 : 0;
+  static constexpr int VS_OFF = 128;
+  static constexpr uint32_t TX = KT + VT + (I8 ? 128 : 0);  // bytes delivered per stage
   static constexpr int NS = D / 32;                 // 8-value K loads per token per lane
   static constexpr int MT = D / 16;                 // PV m-tiles (head_dim rows)
   static constexpr int NT = GT / 8;                 // PV n-tiles (heads)
@@ -361,14 +364,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         if constexpr (I8) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
           bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
-          bulk_g2s(sd + 64, a.vs_base + (size_t)row * kSubTokens, 64, bar);
+          bulk_g2s(sd + C::VS_OFF, a.vs_base + (size_t)row * kSubTokens, 64, bar);
         }
       } else {
         tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
         if constexpr (I8) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
           tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
-          tma_load_2d(sd + 64, &tm_vs, bar, sub * kSubTokens, row);
+          tma_load_2d(sd + C::VS_OFF, &tm_vs, bar, sub * kSubTokens, row);
         }
       }
     }
@@ -583,7 +586,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         }
       }
       if constexpr (I8) {
-        const float4 vs = lds128f(sb + 64 + 16 * r);
+        const float4 vs = lds128f(sb + C::VS_OFF + 16 * r);
         const float vsc[4] = {vs.x, vs.y, vs.z, vs.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {

@@ -202,7 +202,7 @@ def decode_partial(q, k_cache, v_cache, block_table, context_lens, scale, block_
     int8 = k_scales is not None or k_cache.dtype == torch.int8
     B, H, KVH, D, NB = _check_decode_args(None, q, k_cache, v_cache, block_table, context_lens,
                                           block_size, int8, k_scales, v_scales, validate=False)
-    per = partial_floats(H, KVH, D) // KVH * KVH
+    per = partial_floats(H, KVH, D) * KVH  # floats per sequence: kv_heads x head tiles x slot
     if partials is None:
         partials = torch.empty(B, per, dtype=torch.float32, device=q.device)
     _require(partials.dtype == torch.float32 and partials.is_contiguous() and
@@ -234,6 +234,10 @@ def merge_partials(out, partials, num_heads, num_kv_heads):
     P, B = partials.shape[0], partials.shape[1]
     _require(tuple(out.shape) == (B, num_heads, HEAD_DIM) and out.dtype == torch.float16,
              "out must be fp16 [num_seqs, num_heads, head_dim]")
+    per = partial_floats(num_heads, num_kv_heads, HEAD_DIM) * num_kv_heads
+    _require(per > 0 and partials.numel() == P * B * per,
+             "partials must be fp32 [num_parts, num_seqs, per_seq_floats]")
+    _require(partials.device == out.device, "partials and out must be on the same device")
     with _Guard(out.device):
         ws = workspace(out.device, 256)
         rc = _lib.lib().pa_merge_partials(out.data_ptr(), partials.data_ptr(), P, B, num_heads,
