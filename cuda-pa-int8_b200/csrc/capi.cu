@@ -209,6 +209,9 @@ int make_shape(int kv_i8, int mode, int B, int H, int KVH, int D, int bs, int ma
   // stay below 2^31.
   long long per_seq = subpages * s->SEGS;
   long long cb = pa::kBMax;
+  if (s->SEGS > pa::kCounterCap)
+    return fail(PA_ERR_UNSUPPORTED, "too many kv-head segments per sequence (%d)", s->SEGS);
+  if (cb * s->SEGS > pa::kCounterCap) cb = pa::kCounterCap / s->SEGS;
   while (cb > 1 && cb * per_seq >= (1LL << 31)) cb >>= 1;
   if (per_seq >= (1LL << 31)) return fail(PA_ERR_UNSUPPORTED, "context too long for one launch");
   s->chunk_b = (int)cb;
@@ -219,9 +222,7 @@ int make_shape(int kv_i8, int mode, int B, int H, int KVH, int D, int bs, int ma
 
 size_t ws_bytes_for(const Shape& s, int mode, int B) {
   const long long cb = B < s.chunk_b ? B : s.chunk_b;
-  size_t off = pa::kWsHeader;
-  size_t counters = (size_t)(cb > 0 ? cb : 1) * s.SEGS * sizeof(int);
-  off += (counters + 255) / 256 * 256;
+  const size_t off = pa::kWsPartOffset;
   size_t parts;
   if (mode == pa::kModeSplit) {
     parts = (size_t)(cb > 0 ? cb : 1) * s.SEGS * s.s_max * s.SLOT * sizeof(float);
@@ -278,9 +279,7 @@ int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int* status = reinterpret_cast<int*>(ws);
   int* counters = reinterpret_cast<int*>(ws + pa::kWsHeader);
-  const long long cbmax = B < s.chunk_b ? B : s.chunk_b;
-  size_t coff = pa::kWsHeader + ((size_t)cbmax * s.SEGS * sizeof(int) + 255) / 256 * 256;
-  float* part = reinterpret_cast<float*>(ws + coff);
+  float* part = reinterpret_cast<float*>(ws + pa::kWsPartOffset);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   for (int c0 = 0; c0 < B; c0 += s.chunk_b) {

@@ -15,6 +15,11 @@ constexpr int kBMax = 1024;       // sequences per decode launch (the host split
 constexpr int kSubTokens = 16;    // tokens per tensor-core tile ("subpage")
 constexpr int kSplitPages = 32;   // split-K partition: 512 tokens = 32 subpages
 constexpr int kWsHeader = 256;    // workspace bytes before the counters (status word first)
+// Arrival counters occupy a fixed region right after the header, whatever the call shape, so
+// a workspace reused across shapes always presents zeroed counters (each launch leaves the
+// counters it used at zero). Batches are split so that sequences x segments fit.
+constexpr int kCounterCap = 1 << 18;
+constexpr size_t kWsPartOffset = kWsHeader + sizeof(int) * (size_t)kCounterCap;
 
 enum DecodeMode : int {
   kModeStream = 0,    // single pass: page-balanced ranges, fused LSE combine, fp16 out
