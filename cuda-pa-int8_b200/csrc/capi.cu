@@ -202,7 +202,7 @@ int make_shape(int kv_i8, int mode, int B, int H, int KVH, int D, int bs, int ma
   s->SLOT = pa::slot_floats(D, s->GT);
   const long long subpages = ((long long)max_blocks * bs + pa::kSubTokens - 1) / pa::kSubTokens;
   s->s_max = (int)((subpages + pa::kSplitPages - 1) / pa::kSplitPages);
-  s->warps_per_cta = pa::decode_warps_per_cta(kv_i8);
+  s->warps_per_cta = pa::decode_warps_per_cta(kv_i8, s->GT);
   s->sms = num_sms_current(nullptr);
   if (s->sms <= 0) return fail(PA_ERR_CUDA, "cannot query the current device");
   // Sequences per launch: the in-kernel scan holds kBMax, and the flattened page count must

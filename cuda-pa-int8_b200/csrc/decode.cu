@@ -44,6 +44,9 @@ __device__ __forceinline__ int chunk_i8(int r, int si) {
 }
 __device__ __forceinline__ int chunk_f16(int r, int si) { return r + 4 * si; }
 
+// Offset of the 16 V scales inside an INT8 stage's scale tile (K scales sit at 0).
+constexpr int kVsOff = 128;
+
 template <int KVK, int D, int GT, int DEPTH, int WARPS>
 struct Tile {
   static constexpr bool I8 = KVK == 1;
@@ -53,7 +56,6 @@ struct Tile {
   // Scale tiles: 16 K scales at +0 and 16 V scales at +128 (tensor-copy destinations are
   // kept 128-byte aligned); 128 bytes of them are transferred per stage.
   static constexpr int ST = I8 ? 256 : 0;
-  static constexpr int VS_OFF = 128;
   static constexpr uint32_t TX = KT + VT + (I8 ? 128 : 0);  // bytes delivered per stage
   static constexpr int NS = D / 32;                 // 8-value K loads per token per lane
   static constexpr int MT = D / 16;                 // PV m-tiles (head_dim rows)
@@ -364,14 +366,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         if constexpr (I8) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
           bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
-          bulk_g2s(sd + C::VS_OFF, a.vs_base + (size_t)row * kSubTokens, 64, bar);
+          bulk_g2s(sd + kVsOff, a.vs_base + (size_t)row * kSubTokens, 64, bar);
         }
       } else {
         tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
         if constexpr (I8) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
           tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
-          tma_load_2d(sd + C::VS_OFF, &tm_vs, bar, sub * kSubTokens, row);
+          tma_load_2d(sd + kVsOff, &tm_vs, bar, sub * kSubTokens, row);
         }
       }
     }
@@ -389,10 +391,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   int piece_sp0 = csp;
   const float qs = a.qk_scale_log2;
 
-  uint4 qa[NS], qb[NS], qna[NS], qnb[NS];
-  int q_b = -1, q_seg = -1, qn_b = -1, qn_seg = -1;
+  uint4 qa[NS], qb[NS];
+  int q_b = -1, q_seg = -1;
 
-  auto load_q = [&](int b, int seg, uint4 (&xa)[NS], uint4 (&xb)[NS]) {
+  auto load_q = [&](int b, int seg) {
     const int kvh = seg / a.HT;
     const int ht = seg - kvh * a.HT;
     const int hl = ht * GT + g;
@@ -400,16 +402,30 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll
     for (int si = 0; si < NS; ++si) {
       const int c = I8 ? chunk_i8(r, si) : chunk_f16(r, si);
-      xa[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
+      qa[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
                           : make_uint4(0u, 0u, 0u, 0u);
       if constexpr (GT == 16) {
-        xb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
+        qb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
                                 : make_uint4(0u, 0u, 0u, 0u);
       } else {
-        xb[si] = make_uint4(0u, 0u, 0u, 0u);
+        qb[si] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
   };
+
+  // Shared-memory offset of the K cell (chunk of load si, token of n-tile jt) this lane reads.
+  auto koff = [&](int si, int jt) -> uint32_t {
+    const int tau = 4 * (g >> 1) + (g & 1) + 2 * jt;
+    if constexpr (I8) {
+      const int c = chunk_i8(r, si);
+      return c * 128 + ((((tau >> 1) ^ (c & 7)) << 4) | ((tau & 1) << 3));
+    } else {
+      const int c = chunk_f16(r, si);
+      const int row = 2 * c + (tau >> 3);
+      return row * 128 + (((tau & 7) ^ (row & 7)) << 4);
+    }
+  };
+  const uint32_t voff = I8 ? (uint32_t)(g * 16 + 4 * r) : (uint32_t)((g * 16 + 4 * r) * 2);
 
   float m0 = neg_inf(), l0 = 0.f, m1 = neg_inf(), l1 = 0.f;
   float oacc[MT][NT][4];
@@ -423,15 +439,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                       (split && (csp % kSplitPages) == kSplitPages - 1);
     if (first) {
       if (q_b != cb || q_seg != cseg) {
-        if (qn_b == cb && qn_seg == cseg) {
-#pragma unroll
-          for (int si = 0; si < NS; ++si) {
-            qa[si] = qna[si];
-            qb[si] = qnb[si];
-          }
-        } else {
-          load_q(cb, cseg, qa, qb);
-        }
+        load_q(cb, cseg);
         q_b = cb;
         q_seg = cseg;
       }
@@ -447,77 +455,94 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           for (int e = 0; e < 4; ++e) oacc[i][nt][e] = 0.f;
       piece_sp0 = csp;
     }
-    if (last && j + 1 < n) {
-      // Prefetch q of the next segment so the next piece does not wait on it.
-      int nb = cb, nseg = cseg, nsp = csp + 1;
-      if (nsp == cpg) {
-        nsp = 0;
-        if (++nseg == SEGS) {
-          nseg = 0;
-          do { ++nb; } while (pages_of(nb) == 0);
-        }
-      }
-      if ((nb != cb || nseg != cseg) && (nb != qn_b || nseg != qn_seg)) {
-        load_q(nb, nseg, qna, qnb);
-        qn_b = nb;
-        qn_seg = nseg;
-      }
-    }
 
     if (!mbar_wait_bounded(&wbar[s], (uint32_t)(j / DEPTH) & 1u, a.status)) {
       jfail = j;
       break;
     }
 
-    // ---- one 16-token subpage -----------------------------------------------------------------
-    {
-      const int valid = min(kSubTokens, s_ctx[cb] - csp * kSubTokens);
-      const uint32_t kb = smem_u32(k_tiles + (warp * DEPTH + s) * C::KT);
-      const uint32_t vb = smem_u32(v_tiles + (warp * DEPTH + s) * C::VT);
-      const uint32_t sb = I8 ? smem_u32(s_tiles + (warp * DEPTH + s) * C::ST) : 0u;
+    // ---- stage -> registers, then hand the stage back to the TMA right away -------------------
+    const int valid = min(kSubTokens, s_ctx[cb] - csp * kSubTokens);
+    const uint32_t kb = smem_u32(k_tiles + (warp * DEPTH + s) * C::KT);
+    const uint32_t vb = smem_u32(v_tiles + (warp * DEPTH + s) * C::VT);
+    const uint32_t sb = I8 ? smem_u32(s_tiles + (warp * DEPTH + s) * C::ST) : 0u;
+    // K: INT8 8 bytes per (si, jt) cell; FP16 16 bytes.
+    uint2 k8[NS][2];
+    uint4 k16[NS][2];
+    uint32_t v8[MT][2];
+    uint2 v16[MT][2];
+    float4 ksv = make_float4(0.f, 0.f, 0.f, 0.f), vsv = ksv;
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+#pragma unroll
+      for (int jt = 0; jt < 2; ++jt) {
+        if constexpr (I8) k8[si][jt] = lds64(kb + koff(si, jt));
+        else k16[si][jt] = lds128(kb + koff(si, jt));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      if constexpr (I8) {
+        v8[i][0] = lds32(vb + voff + i * 256);
+        v8[i][1] = lds32(vb + voff + i * 256 + 128);
+      } else {
+        v16[i][0] = lds64(vb + voff + i * 512);
+        v16[i][1] = lds64(vb + voff + i * 512 + 256);
+      }
+    }
+    if constexpr (I8) {
+      ksv = lds128f(sb + 16 * r);
+      vsv = lds128f(sb + kVsOff + 16 * r);
+    }
+    __syncwarp();
+    if (j + DEPTH < n) {
+      if (lane == 0) fence_proxy_async_smem();
+      issue(j + DEPTH);
+      ++issued;
+    }
 
-      // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n).
-      float sacc[2][4];
+    // ---- one 16-token subpage from registers ---------------------------------------------------
+    {
+      // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n). Two accumulation
+      // chains per n-tile (even / odd si) shorten the dependent MMA sequence.
+      float sacc[2][2][4];
 #pragma unroll
       for (int jt = 0; jt < 2; ++jt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sacc[jt][e] = 0.f;
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sacc[jt][hh][e] = 0.f;
 #pragma unroll
       for (int si = 0; si < NS; ++si) {
 #pragma unroll
         for (int jt = 0; jt < 2; ++jt) {
-          const int tau = 4 * (g >> 1) + (g & 1) + 2 * jt;
           uint32_t b0a, b1a, b0b, b1b;
           if constexpr (I8) {
-            const int c = chunk_i8(r, si);
-            const uint2 kw =
-                lds64(kb + c * 128 + ((((tau >> 1) ^ (c & 7)) << 4) | ((tau & 1) << 3)));
-            i8x4_to_f16x2x2(kw.x, b0a, b1a);
-            i8x4_to_f16x2x2(kw.y, b0b, b1b);
+            i8x4_to_f16x2x2(k8[si][jt].x, b0a, b1a);
+            i8x4_to_f16x2x2(k8[si][jt].y, b0b, b1b);
           } else {
-            const int c = chunk_f16(r, si);
-            const int row = 2 * c + (tau >> 3);
-            const uint4 kw = lds128(kb + row * 128 + (((tau & 7) ^ (row & 7)) << 4));
-            b0a = kw.x;
-            b1a = kw.y;
-            b0b = kw.z;
-            b1b = kw.w;
+            b0a = k16[si][jt].x;
+            b1a = k16[si][jt].y;
+            b0b = k16[si][jt].z;
+            b1b = k16[si][jt].w;
           }
-          mma_16816(sacc[jt], qa[si].x, qb[si].x, qa[si].y, qb[si].y, b0a, b1a);
-          mma_16816(sacc[jt], qa[si].z, qb[si].z, qa[si].w, qb[si].w, b0b, b1b);
+          float (&acc)[4] = sacc[jt][si & 1];
+          mma_16816(acc, qa[si].x, qb[si].x, qa[si].y, qb[si].y, b0a, b1a);
+          mma_16816(acc, qa[si].z, qb[si].z, qa[si].w, qb[si].w, b0b, b1b);
         }
       }
 
       // Scores of tokens 4r..4r+3 for heads g (x) and g+8 (y), in log2 units.
-      float x[4] = {sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]};
-      float y[4] = {sacc[0][2], sacc[0][3], sacc[1][2], sacc[1][3]};
+      float x[4] = {sacc[0][0][0] + sacc[0][1][0], sacc[0][0][1] + sacc[0][1][1],
+                    sacc[1][0][0] + sacc[1][1][0], sacc[1][0][1] + sacc[1][1][1]};
+      float y[4] = {sacc[0][0][2] + sacc[0][1][2], sacc[0][0][3] + sacc[0][1][3],
+                    sacc[1][0][2] + sacc[1][1][2], sacc[1][0][3] + sacc[1][1][3]};
       float ksc[4] = {qs, qs, qs, qs};
       if constexpr (I8) {
-        const float4 ks = lds128f(sb + 16 * r);
-        ksc[0] = ks.x * qs;
-        ksc[1] = ks.y * qs;
-        ksc[2] = ks.z * qs;
-        ksc[3] = ks.w * qs;
+        ksc[0] = ksv.x * qs;
+        ksc[1] = ksv.y * qs;
+        ksc[2] = ksv.z * qs;
+        ksc[3] = ksv.w * qs;
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -586,8 +611,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         }
       }
       if constexpr (I8) {
-        const float4 vs = lds128f(sb + C::VS_OFF + 16 * r);
-        const float vsc[4] = {vs.x, vs.y, vs.z, vs.w};
+        const float vsc[4] = {vsv.x, vsv.y, vsv.z, vsv.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const bool ok = (4 * r + e) < valid;
@@ -610,29 +634,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       for (int i = 0; i < MT; ++i) {
         uint32_t a0, a1, a2, a3;
         if constexpr (I8) {
-          const uint32_t wa = lds32(vb + (16 * i + g) * 16 + 4 * r);
-          const uint32_t wb = lds32(vb + (16 * i + g + 8) * 16 + 4 * r);
-          i8x4_to_f16x2x2(wa, a0, a2);
-          i8x4_to_f16x2x2(wb, a1, a3);
+          i8x4_to_f16x2x2(v8[i][0], a0, a2);
+          i8x4_to_f16x2x2(v8[i][1], a1, a3);
         } else {
-          const uint2 wa = lds64(vb + ((16 * i + g) * 16 + 4 * r) * 2);
-          const uint2 wb = lds64(vb + ((16 * i + g + 8) * 16 + 4 * r) * 2);
-          a0 = wa.x & mlo;
-          a2 = wa.y & mhi;
-          a1 = wb.x & mlo;
-          a3 = wb.y & mhi;
+          a0 = v16[i][0].x & mlo;
+          a2 = v16[i][0].y & mhi;
+          a1 = v16[i][1].x & mlo;
+          a3 = v16[i][1].y & mhi;
         }
         mma_16816(oacc[i][0], a0, a1, a2, a3, pb0, pb1);
         if constexpr (NT == 2) mma_16816(oacc[i][1], a0, a1, a2, a3, pc0, pc1);
       }
-    }
-
-    // Release the stage and refill it with the page DEPTH ahead.
-    __syncwarp();
-    if (j + DEPTH < n) {
-      if (lane == 0) fence_proxy_async_smem();
-      issue(j + DEPTH);
-      ++issued;
     }
 
     if (last) {
@@ -796,15 +808,32 @@ __global__ void __launch_bounds__(128) reduce_kernel(const ReduceArgs a) {
                         hcnt, orow, nullptr, a.status);
 }
 
-// Tuned shapes: INT8 stages are 4.2 KB, FP16 stages 8 KB.
-constexpr int kWarpsI8 = 8, kDepthI8 = 4;
-constexpr int kWarpsF16 = 8, kDepthF16 = 3;
+// Launch shapes per (cache dtype, head tile): warps per CTA (one CTA per SM) and ring depth
+// per warp. A stage is held only while its bytes are read into registers, so all DEPTH
+// stages of a warp are in flight while it computes.
+#ifndef PA_I8_WARPS
+#define PA_I8_WARPS 16
+#endif
+#ifndef PA_I8_DEPTH
+#define PA_I8_DEPTH 3
+#endif
+#ifndef PA_F16_WARPS
+#define PA_F16_WARPS 12
+#endif
+#ifndef PA_F16_DEPTH
+#define PA_F16_DEPTH 2
+#endif
+template <int KVK, int GT> struct Shape;
+template <> struct Shape<1, 8> { static constexpr int W = PA_I8_WARPS, DP = PA_I8_DEPTH; };
+template <> struct Shape<0, 8> { static constexpr int W = PA_F16_WARPS, DP = PA_F16_DEPTH; };
+template <> struct Shape<1, 16> { static constexpr int W = 8, DP = 4; };
+template <> struct Shape<0, 16> { static constexpr int W = 8, DP = 3; };
 
 template <int KVK, int GT>
 cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
                        cudaStream_t stream) {
-  constexpr int W = KVK ? kWarpsI8 : kWarpsF16;
-  constexpr int DP = KVK ? kDepthI8 : kDepthF16;
+  constexpr int W = Shape<KVK, GT>::W;
+  constexpr int DP = Shape<KVK, GT>::DP;
   using C = Tile<KVK, 128, GT, DP, W>;
   auto kern = decode_kernel<KVK, 128, GT, DP, W>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -816,15 +845,9 @@ cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
 
 }  // namespace
 
-int decode_warps_per_cta(int kv_i8) { return kv_i8 ? kWarpsI8 : kWarpsF16; }
-
-size_t decode_smem_bytes(int kv_i8, int gt) {
-  if (kv_i8) {
-    return gt == 8 ? Tile<1, 128, 8, kDepthI8, kWarpsI8>::SMEM
-                   : Tile<1, 128, 16, kDepthI8, kWarpsI8>::SMEM;
-  }
-  return gt == 8 ? Tile<0, 128, 8, kDepthF16, kWarpsF16>::SMEM
-                 : Tile<0, 128, 16, kDepthF16, kWarpsF16>::SMEM;
+int decode_warps_per_cta(int kv_i8, int gt) {
+  if (kv_i8) return gt == 8 ? Shape<1, 8>::W : Shape<1, 16>::W;
+  return gt == 8 ? Shape<0, 8>::W : Shape<0, 16>::W;
 }
 
 cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensorMap* maps,

@@ -62,7 +62,7 @@ struct ReduceArgs {
 cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensorMap* maps,
                           int grid, cudaStream_t stream);
 cudaError_t launch_reduce(int gt, const ReduceArgs& a, cudaStream_t stream);
-int decode_warps_per_cta(int kv_i8);
+int decode_warps_per_cta(int kv_i8, int gt);
 cudaError_t launch_write_rows(int in_dtype, bool i8, int D, const void* k, const void* v,
                               long long token_stride, const int* slots, int N, int KVH,
                               void* kc, void* vc, float* ks, float* vs, int NB, int bs,
@@ -75,7 +75,6 @@ cudaError_t launch_prefill(int in_dtype, bool i8, const void* k, const void* v, 
 cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float* scale_out,
                                 int semantics, unsigned int* scratch, int num_sms,
                                 cudaStream_t st);
-size_t decode_smem_bytes(int kv_i8, int gt);
 
 // Partial slot size in floats: O[D][GT] + m[GT] + l[GT].
 inline int slot_floats(int head_dim, int gt) { return (head_dim + 2) * gt; }
