@@ -310,10 +310,10 @@ int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
     a.s_max = s.s_max;
     a.bulk = bulk ? 1 : 0;
     a.qk_scale_log2 = scale * 1.4426950408889634f;
-    // Grid: one CTA per SM, fewer when the batch is small (at least ~8 subpages per warp).
+    // Grid: one CTA per SM; fewer only when there are fewer subpages than warps.
     const long long subpages = ((long long)max_blocks * bs + pa::kSubTokens - 1) / pa::kSubTokens;
     const long long t_max = (long long)nb * s.SEGS * subpages;
-    long long want = (t_max + 8LL * s.warps_per_cta - 1) / (8LL * s.warps_per_cta);
+    long long want = (t_max + s.warps_per_cta - 1) / s.warps_per_cta;
     if (want < 1) want = 1;
     const int grid = (int)(want < s.sms ? want : s.sms);
     a.total_warps = grid * s.warps_per_cta;

@@ -30,6 +30,7 @@
 #include "pa_common.cuh"
 #include "pa_internal.h"
 
+#include <atomic>
 #include <cstdio>
 
 namespace pa {
@@ -68,48 +69,89 @@ struct Tile {
 // ---------------------------------------------------------------------------------------
 // Warp-level log-sum-exp merge of `np` partial slots into either fp16 output rows
 // (out_rows[h * D + d]) or one merged partial slot (out_slot). Slot layout: O[D][GT], m[GT],
-// l[GT]; lane owns head_dim rows [lane*D/32, (lane+1)*D/32).
+// l[GT]. The running maxima and the denominators are formed lane-parallel (lane k reads
+// piece k), then the O rows are accumulated two pieces at a time so that their loads are in
+// flight together; lane owns head_dim rows [lane*D/32, (lane+1)*D/32).
 // ---------------------------------------------------------------------------------------
 template <int D, int GT, typename PieceFn>
 __device__ __forceinline__ void combine_pieces(PieceFn piece, int np, int lane, int hcnt,
                                                __half* out_rows, float* out_slot,
                                                int* status) {
   constexpr int DPL = D / 32;
-  float M[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) M[h] = neg_inf();
-  for (int k = 0; k < np; ++k) {
-    const float* sl = piece(k);
-#pragma unroll
-    for (int h = 0; h < GT; ++h) M[h] = fmaxf(M[h], __ldcg(sl + D * GT + h));
-  }
-  float L[GT];
-  float acc[DPL][GT];
+  constexpr int Q = DPL * GT / 4;  // float4 loads per lane per piece
+  float M[GT], L[GT];
 #pragma unroll
   for (int h = 0; h < GT; ++h) {
+    M[h] = neg_inf();
     L[h] = 0.f;
-#pragma unroll
-    for (int dd = 0; dd < DPL; ++dd) acc[dd][h] = 0.f;
   }
-  for (int k = 0; k < np; ++k) {
-    const float* sl = piece(k);
-    float wgt[GT];
+  for (int k = lane; k < np; k += 32) {
+    const float4* mk = reinterpret_cast<const float4*>(piece(k) + D * GT);
+#pragma unroll
+    for (int h4 = 0; h4 < GT / 4; ++h4) {
+      const float4 v = __ldcg(mk + h4);
+      M[4 * h4 + 0] = fmaxf(M[4 * h4 + 0], v.x);
+      M[4 * h4 + 1] = fmaxf(M[4 * h4 + 1], v.y);
+      M[4 * h4 + 2] = fmaxf(M[4 * h4 + 2], v.z);
+      M[4 * h4 + 3] = fmaxf(M[4 * h4 + 3], v.w);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < GT; ++h) M[h] = warp_max(M[h]);
+  for (int k = lane; k < np; k += 32) {
+    const float* sl = piece(k) + D * GT;
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
-      const float mk = __ldcg(sl + D * GT + h);
-      wgt[h] = (M[h] == neg_inf()) ? 0.f : ex2(mk - M[h]);
-      L[h] += wgt[h] * __ldcg(sl + D * GT + GT + h);
+      const float mk = __ldcg(sl + h);
+      const float w = (M[h] == neg_inf()) ? 0.f : ex2(mk - M[h]);
+      L[h] += w * __ldcg(sl + GT + h);
     }
-    const float4* rows = reinterpret_cast<const float4*>(sl + lane * DPL * GT);
+  }
 #pragma unroll
-    for (int dd = 0; dd < DPL; ++dd) {
+  for (int h = 0; h < GT; ++h) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L[h] += __shfl_xor_sync(0xffffffffu, L[h], o);
+  }
+
+  // Pieces accumulated per step (their loads are in flight together); bounded by registers.
+  constexpr int U = GT == 8 ? 2 : 1;
+  float acc[DPL * GT];
+#pragma unroll
+  for (int i = 0; i < DPL * GT; ++i) acc[i] = 0.f;
+  for (int k = 0; k < np; k += U) {
+    float4 v[U][Q];
+    float4 mv[U][GT / 4];
+    bool ok[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      ok[u] = (k + u) < np;
+      const float* sl = piece(ok[u] ? k + u : k);
+#pragma unroll
+      for (int q = 0; q < Q; ++q)
+        v[u][q] = __ldcg(reinterpret_cast<const float4*>(sl + lane * DPL * GT) + q);
+#pragma unroll
+      for (int h4 = 0; h4 < GT / 4; ++h4)
+        mv[u][h4] = __ldcg(reinterpret_cast<const float4*>(sl + D * GT) + h4);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float w[GT];
 #pragma unroll
       for (int h4 = 0; h4 < GT / 4; ++h4) {
-        const float4 v = __ldcg(rows + dd * (GT / 4) + h4);
-        acc[dd][4 * h4 + 0] += wgt[4 * h4 + 0] * v.x;
-        acc[dd][4 * h4 + 1] += wgt[4 * h4 + 1] * v.y;
-        acc[dd][4 * h4 + 2] += wgt[4 * h4 + 2] * v.z;
-        acc[dd][4 * h4 + 3] += wgt[4 * h4 + 3] * v.w;
+        const float a[4] = {mv[u][h4].x, mv[u][h4].y, mv[u][h4].z, mv[u][h4].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = 4 * h4 + e;
+          w[h] = (!ok[u] || M[h] == neg_inf()) ? 0.f : ex2(a[e] - M[h]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        const int h = (4 * q) % GT;
+        acc[4 * q + 0] += w[h + 0] * v[u][q].x;
+        acc[4 * q + 1] += w[h + 1] * v[u][q].y;
+        acc[4 * q + 2] += w[h + 2] * v[u][q].z;
+        acc[4 * q + 3] += w[h + 3] * v[u][q].w;
       }
     }
   }
@@ -125,7 +167,7 @@ __device__ __forceinline__ void combine_pieces(PieceFn piece, int np, int lane, 
         }
         __half tmp[DPL];
 #pragma unroll
-        for (int dd = 0; dd < DPL; ++dd) tmp[dd] = __float2half_rn(acc[dd][h] * inv);
+        for (int dd = 0; dd < DPL; ++dd) tmp[dd] = __float2half_rn(acc[dd * GT + h] * inv);
         __half* dst = out_rows + (size_t)h * D + lane * DPL;
         if constexpr (DPL == 4) {
           *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(tmp);
@@ -138,14 +180,8 @@ __device__ __forceinline__ void combine_pieces(PieceFn piece, int np, int lane, 
   } else {
     float4* rows = reinterpret_cast<float4*>(out_slot + lane * DPL * GT);
 #pragma unroll
-    for (int dd = 0; dd < DPL; ++dd) {
-#pragma unroll
-      for (int h4 = 0; h4 < GT / 4; ++h4) {
-        rows[dd * (GT / 4) + h4] =
-            make_float4(acc[dd][4 * h4], acc[dd][4 * h4 + 1], acc[dd][4 * h4 + 2],
-                        acc[dd][4 * h4 + 3]);
-      }
-    }
+    for (int q = 0; q < Q; ++q)
+      rows[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
     if (lane == 0) {
 #pragma unroll
       for (int h = 0; h < GT; ++h) {
@@ -177,6 +213,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ int s_ctx[kBMax];
   __shared__ int s_tmp[32];
   __shared__ int s_empty;
+  __shared__ int s_pend[WARPS][2][6];
   extern __shared__ __align__(16) uint8_t dsm_raw[];
 
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
@@ -431,6 +468,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   float oacc[MT][NT][4];
 
   int jfail = -1;
+  int npend = 0;
   for (int j = 0; j < n; ++j) {
     const int s = j % DEPTH;
     const bool split = (a.mode == kModeSplit);
@@ -734,21 +772,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         const int wf = (int)(((s_start + 1) * Wt - 1) / T);
         const int wl = (int)((s_end * Wt - 1) / T);
         const int np = wl - wf + 1;
-        if (old == np - 1) {
-          __threadfence();
-          auto piece = [&](int k) -> const float* {
-            const int wk = wf + k;
-            return a.part + ((size_t)wk * 2 + (k == 0 ? 1 : 0)) * SLOT;
-          };
-          if (a.mode == kModeStream) {
-            combine_pieces<D, GT>(piece, np, lane, hcnt,
-                                  a.out + ((size_t)cb * a.H + hbase) * D, nullptr, a.status);
-          } else {
-            combine_pieces<D, GT>(piece, np, lane, hcnt, nullptr,
-                                  a.part_out + (size_t)segid * SLOT, a.status);
-          }
-          if (lane == 0) a.counters[segid] = 0;
+        if (old == np - 1 && lane == 0) {
+          // Last arrival: merge after the page loop, when its registers are free. A warp
+          // finishes at most two split segments (its first and its last).
+          int* pe = s_pend[warp][npend];
+          pe[0] = segid;
+          pe[1] = wf;
+          pe[2] = np;
+          pe[3] = cb;
+          pe[4] = hbase;
+          pe[5] = hcnt;
         }
+        npend += (old == np - 1) ? 1 : 0;
       }
     }
 
@@ -763,6 +798,25 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
       if (j + 1 < n) cpg = pages_of(cb);
     }
+  }
+
+  // Deferred log-sum-exp merges of the segments this warp completed last.
+  __syncwarp();
+  for (int e = 0; e < npend; ++e) {
+    const int* pe = s_pend[warp][e];
+    const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
+    __threadfence();
+    auto piece = [&](int k) -> const float* {
+      return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
+    };
+    if (a.mode == kModeStream) {
+      combine_pieces<D, GT>(piece, np, lane, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
+                            nullptr, a.status);
+    } else {
+      combine_pieces<D, GT>(piece, np, lane, hcnt, nullptr, a.part_out + (size_t)segid * SLOT,
+                            a.status);
+    }
+    if (lane == 0) a.counters[segid] = 0;
   }
 
   if (jfail >= 0) {
@@ -812,13 +866,13 @@ __global__ void __launch_bounds__(128) reduce_kernel(const ReduceArgs a) {
 // per warp. A stage is held only while its bytes are read into registers, so all DEPTH
 // stages of a warp are in flight while it computes.
 #ifndef PA_I8_WARPS
-#define PA_I8_WARPS 16
+#define PA_I8_WARPS 12
 #endif
 #ifndef PA_I8_DEPTH
 #define PA_I8_DEPTH 3
 #endif
 #ifndef PA_F16_WARPS
-#define PA_F16_WARPS 12
+#define PA_F16_WARPS 8
 #endif
 #ifndef PA_F16_DEPTH
 #define PA_F16_DEPTH 2
@@ -836,9 +890,17 @@ cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
   constexpr int DP = Shape<KVK, GT>::DP;
   using C = Tile<KVK, 128, GT, DP, W>;
   auto kern = decode_kernel<KVK, 128, GT, DP, W>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)C::SMEM);
+  // The shared-memory opt-in is a per-device function attribute: set it once per device.
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
   kern<<<grid, W * 32, C::SMEM, stream>>>(a, maps[0], maps[1], maps[2], maps[3]);
   return cudaGetLastError();
 }
