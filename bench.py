@@ -164,7 +164,8 @@ def build_workload(torch, cfg, rank, world, device):
     return w
 
 
-def make_step(torch, w, splitk, validate=False):
+def make_step(torch, w, splitk, validate=False, decode_only=False):
+    """One step of the workload: [one-token quantize-write per sequence +] decode."""
     from pa_b200 import ops
     scale = 1.0 / math.sqrt(HEAD_DIM)
     use_split = splitk or w.cfg == 4
@@ -174,16 +175,14 @@ def make_step(torch, w, splitk, validate=False):
                    BLOCK, k_scales=w.k_scales, v_scales=w.v_scales, splitk=use_split,
                    validate=validate)
 
-    if w.step_tokens:
+    dec_launches = 2 if use_split else 1
+    if w.step_tokens and not decode_only:
         def step():
             ops.quantize_into_cache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.k_scales,
                                     w.v_scales, w.slots, BLOCK)
             decode()
-        launches = 1 + (2 if use_split else 1)
-    else:
-        step = decode
-        launches = 2 if use_split else 1
-    return step, launches
+        return step, 1 + dec_launches
+    return decode, dec_launches
 
 
 # ---------------------------------------------------------------------------------------
@@ -293,6 +292,17 @@ def cpu_baseline(cfg, budget_s=10.0):
                       f"{el:.1f} s"}
 
 
+def profile_traffic(cfg):
+    """DRAM bytes (read + write) per decode launch from the committed ncu summary of this
+    workload (profiles/), or None when there is none."""
+    path = os.path.join(HERE, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(f"cfg{cfg}")
+    except Exception:
+        return None
+
+
 def config_desc(cfg, w, splitk):
     names = {2: "cfg2 FP16 decode B64 ctx4096 32/8 heads",
              3: "cfg3 INT8 per-token decode + 1-token quantize-write B64 ctx8192 12/2",
@@ -344,8 +354,25 @@ def main():
 
     w = build_workload(torch, args.config, rank, world, device)
     step, launches = make_step(torch, w, args.splitk)
-    for _ in range(max(3, args.warmup)):
-        step()
+    decode_only, decode_launches = make_step(torch, w, args.splitk, decode_only=True)
+
+    # Warm up eagerly on the capture stream (its workspace is created here), then capture
+    # the K timed steps into one CUDA graph so that host launch overhead is not measured.
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap):
+        for _ in range(max(3, args.warmup)):
+            step()
+            decode_only()
+    torch.cuda.synchronize()
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step, stream=cap):
+        for _ in range(args.steps):
+            step()
+    g_dec = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_dec, stream=cap):
+        for _ in range(args.steps):
+            decode_only()
     torch.cuda.synchronize()
 
     # Untimed soak so the clock sampler sees the kernel under load, then the timed steps.
@@ -355,8 +382,7 @@ def main():
         time.sleep(0.3)
     t_end = time.perf_counter() + args.soak_ms / 1e3
     while time.perf_counter() < t_end:
-        for _ in range(20):
-            step()
+        g_step.replay()
         torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -364,23 +390,31 @@ def main():
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(args.steps):
-        step()
+    g_step.replay()
     end.record()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     clocks = sampler.stop() if sampler else None
     ms = start.elapsed_time(end) / args.steps
+    # The dominant kernel alone (decode), same device clock, for the roofline figure.
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    d0.record()
+    g_dec.replay()
+    d1.record()
+    torch.cuda.synchronize()
+    dec_ms = d0.elapsed_time(d1) / args.steps
     if dist:
-        t = torch.tensor([ms], device=device)
+        t = torch.tensor([ms, dec_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, dec_ms = float(t[0]), float(t[1])
         tot = torch.tensor([float(w.step_bytes), float(w.B)], device=device, dtype=torch.float64)
         dist.all_reduce(tot)
         total_bytes, total_seqs = float(tot[0]), float(tot[1])
     else:
         total_bytes, total_seqs = float(w.step_bytes), float(w.B)
+    del g_step, g_dec
     from pa_b200 import ops
     status = ops.read_status(device)
 
@@ -436,6 +470,7 @@ def main():
     peak, peak_kind = measured_peak()
     value = total_bytes / (ms * 1e-3) / 1e9
     per_gpu = float(w.step_bytes) / (ms * 1e-3) / 1e9
+    kernel_gbs = float(w.decode_bytes) / (dec_ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -445,9 +480,13 @@ def main():
         "pct_of_nominal_8000": 100.0 * per_gpu / NOMINAL_GBS,
         "pct_of_measured_peak": 100.0 * per_gpu / peak,
         "gpu_launches": launches * args.steps,
-        "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s",
-                     "frac": per_gpu / peak, "peak_kind": peak_kind,
-                     "traffic": None,
+        "timing": "CUDA graph of the K steps, replayed once between CUDA events",
+        "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": kernel_gbs / peak, "peak_kind": peak_kind,
+                     "kernel": "decode (%s)" % ("split-K pair" if (args.splitk or args.config == 4)
+                                                else "single pass"),
+                     "kernel_ms": dec_ms,
+                     "traffic": profile_traffic(args.config),
                      "algorithmic_bytes_per_launch": w.decode_bytes},
         "device_status": status,
         "clocks": clocks,

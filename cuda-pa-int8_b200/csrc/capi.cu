@@ -336,7 +336,7 @@ int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
       ra.num_parts = 0;
       ra.piece_stride = s.SLOT;
       ra.seg_stride = (long long)s.s_max * s.SLOT;
-      e = pa::launch_reduce(s.GT, ra, st);
+      e = pa::launch_reduce(s.GT, ra, s.s_max, st);
       if (e != cudaSuccess) return cuda_fail(e, "reduce launch");
     }
   }
@@ -493,7 +493,7 @@ int pa_merge_partials(void* out, const float* partials, int num_parts, int num_s
   ra.num_parts = num_parts;
   ra.piece_stride = (long long)num_seqs * num_kv_heads * HT * SLOT;
   ra.seg_stride = SLOT;
-  cudaError_t e = pa::launch_reduce(GT, ra, static_cast<cudaStream_t>(stream));
+  cudaError_t e = pa::launch_reduce(GT, ra, num_parts, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   return PA_OK;
 }

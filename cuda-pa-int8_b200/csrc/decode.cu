@@ -67,129 +67,173 @@ struct Tile {
 };
 
 // ---------------------------------------------------------------------------------------
-// Warp-level log-sum-exp merge of `np` partial slots into either fp16 output rows
-// (out_rows[h * D + d]) or one merged partial slot (out_slot). Slot layout: O[D][GT], m[GT],
-// l[GT]. The running maxima and the denominators are formed lane-parallel (lane k reads
-// piece k), then the O rows are accumulated two pieces at a time so that their loads are in
-// flight together; lane owns head_dim rows [lane*D/32, (lane+1)*D/32).
+// CTA-cooperative log-sum-exp merge of `np` partial slots (all NTHR threads of the block take
+// part; scratch is shared memory). Pass 1 forms the maxima, the per-piece weights (kept in
+// shared memory) and the denominators with every thread reading a different piece; pass 2
+// gives each thread one float4 of the [D][GT] output and U pieces' loads in flight per step,
+// so a merge costs a handful of dependent L2 round trips however many pieces there are.
 // ---------------------------------------------------------------------------------------
-template <int D, int GT, typename PieceFn>
-__device__ __forceinline__ void combine_pieces(PieceFn piece, int np, int lane, int hcnt,
-                                               __half* out_rows, float* out_slot,
-                                               int* status) {
-  constexpr int DPL = D / 32;
-  constexpr int Q = DPL * GT / 4;  // float4 loads per lane per piece
-  float M[GT], L[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    M[h] = neg_inf();
-    L[h] = 0.f;
+template <int D, int GT, int NTHR, int U>
+struct Coop {
+  static constexpr int OUT4 = D * GT / 4;                        // float4 outputs
+  static constexpr int PG = NTHR >= OUT4 ? NTHR / OUT4 : 1;      // piece groups
+  static constexpr int OPT = NTHR >= OUT4 ? 1 : OUT4 / NTHR;     // outputs per thread
+  static constexpr int NW = NTHR / 32;
+  // Scratch floats needed for np pieces.
+  __host__ __device__ static constexpr size_t floats(int np) {
+    return 2 * GT + NW * GT + ((size_t)np * GT + 3) / 4 * 4 + (size_t)PG * OUT4 * 4;
   }
-  for (int k = lane; k < np; k += 32) {
+};
+
+template <int D, int GT, int NTHR, int U, typename PieceFn>
+__device__ __forceinline__ void coop_combine(PieceFn piece, int np, int hcnt, __half* out_rows,
+                                             float* out_slot, int* status, float* sm) {
+  using CC = Coop<D, GT, NTHR, U>;
+  static_assert(NTHR >= CC::OUT4 || CC::OUT4 % NTHR == 0, "outputs must tile the block");
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  float* sM = sm;
+  float* sL = sm + GT;
+  float* sRed = sm + 2 * GT;
+  float* sW = sRed + CC::NW * GT;
+  float4* sAcc = reinterpret_cast<float4*>(sW + ((size_t)np * GT + 3) / 4 * 4);
+
+  float mx[GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) mx[h] = neg_inf();
+  for (int k = tid; k < np; k += NTHR) {
     const float4* mk = reinterpret_cast<const float4*>(piece(k) + D * GT);
 #pragma unroll
     for (int h4 = 0; h4 < GT / 4; ++h4) {
       const float4 v = __ldcg(mk + h4);
-      M[4 * h4 + 0] = fmaxf(M[4 * h4 + 0], v.x);
-      M[4 * h4 + 1] = fmaxf(M[4 * h4 + 1], v.y);
-      M[4 * h4 + 2] = fmaxf(M[4 * h4 + 2], v.z);
-      M[4 * h4 + 3] = fmaxf(M[4 * h4 + 3], v.w);
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < GT; ++h) M[h] = warp_max(M[h]);
-  for (int k = lane; k < np; k += 32) {
-    const float* sl = piece(k) + D * GT;
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      const float mk = __ldcg(sl + h);
-      const float w = (M[h] == neg_inf()) ? 0.f : ex2(mk - M[h]);
-      L[h] += w * __ldcg(sl + GT + h);
+      mx[4 * h4 + 0] = fmaxf(mx[4 * h4 + 0], v.x);
+      mx[4 * h4 + 1] = fmaxf(mx[4 * h4 + 1], v.y);
+      mx[4 * h4 + 2] = fmaxf(mx[4 * h4 + 2], v.z);
+      mx[4 * h4 + 3] = fmaxf(mx[4 * h4 + 3], v.w);
     }
   }
 #pragma unroll
   for (int h = 0; h < GT; ++h) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) L[h] += __shfl_xor_sync(0xffffffffu, L[h], o);
+    const float v = warp_max(mx[h]);
+    if (lane == 0) sRed[warp * GT + h] = v;
   }
-
-  // Pieces accumulated per step (their loads are in flight together); bounded by registers.
-  constexpr int U = GT == 8 ? 2 : 1;
-  float acc[DPL * GT];
+  __syncthreads();
+  if (tid < GT) {
+    float v = neg_inf();
+    for (int w = 0; w < CC::NW; ++w) v = fmaxf(v, sRed[w * GT + tid]);
+    sM[tid] = v;
+  }
+  __syncthreads();
+  float ls[GT];
 #pragma unroll
-  for (int i = 0; i < DPL * GT; ++i) acc[i] = 0.f;
-  for (int k = 0; k < np; k += U) {
-    float4 v[U][Q];
-    float4 mv[U][GT / 4];
-    bool ok[U];
+  for (int h = 0; h < GT; ++h) ls[h] = 0.f;
+  for (int k = tid; k < np; k += NTHR) {
+    const float4* mk = reinterpret_cast<const float4*>(piece(k) + D * GT);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      ok[u] = (k + u) < np;
-      const float* sl = piece(ok[u] ? k + u : k);
+    for (int h4 = 0; h4 < GT / 4; ++h4) {
+      const float4 m4 = __ldcg(mk + h4);
+      const float4 l4 = __ldcg(mk + GT / 4 + h4);
+      const float mm[4] = {m4.x, m4.y, m4.z, m4.w};
+      const float ll[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
-      for (int q = 0; q < Q; ++q)
-        v[u][q] = __ldcg(reinterpret_cast<const float4*>(sl + lane * DPL * GT) + q);
-#pragma unroll
-      for (int h4 = 0; h4 < GT / 4; ++h4)
-        mv[u][h4] = __ldcg(reinterpret_cast<const float4*>(sl + D * GT) + h4);
+      for (int e = 0; e < 4; ++e) {
+        const int h = 4 * h4 + e;
+        const float M = sM[h];
+        const float w = (M == neg_inf()) ? 0.f : ex2(mm[e] - M);
+        sW[(size_t)k * GT + h] = w;
+        ls[h] += w * ll[e];
+      }
     }
+  }
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      float w[GT];
+  for (int h = 0; h < GT; ++h) {
+    float v = ls[h];
 #pragma unroll
-      for (int h4 = 0; h4 < GT / 4; ++h4) {
-        const float a[4] = {mv[u][h4].x, mv[u][h4].y, mv[u][h4].z, mv[u][h4].w};
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) sRed[warp * GT + h] = v;
+  }
+  __syncthreads();
+  if (tid < GT) {
+    float v = 0.f;
+    for (int w = 0; w < CC::NW; ++w) v += sRed[w * GT + tid];
+    sL[tid] = v;
+  }
+  __syncthreads();
+
+  const int pg = (NTHR >= CC::OUT4) ? tid / CC::OUT4 : 0;
+  float4 acc[CC::OPT];
+#pragma unroll
+  for (int i = 0; i < CC::OPT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (pg < CC::PG) {
+#pragma unroll
+    for (int i = 0; i < CC::OPT; ++i) {
+      const int o = (NTHR >= CC::OUT4) ? tid % CC::OUT4 : tid + i * NTHR;
+      const int h0 = (o % (GT / 4)) * 4;
+      for (int k0 = pg; k0 < np; k0 += CC::PG * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int k = k0 + u * CC::PG;
+          v[u] = (k < np) ? __ldcg(reinterpret_cast<const float4*>(piece(k)) + o)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int k = k0 + u * CC::PG;
+          if (k < np) {
+            const float* w = sW + (size_t)k * GT + h0;
+            acc[i].x += w[0] * v[u].x;
+            acc[i].y += w[1] * v[u].y;
+            acc[i].z += w[2] * v[u].z;
+            acc[i].w += w[3] * v[u].w;
+          }
+        }
+      }
+    }
+  }
+  if constexpr (CC::PG > 1) {
+    if (pg < CC::PG) sAcc[pg * CC::OUT4 + tid % CC::OUT4] = acc[0];
+    __syncthreads();
+    if (pg == 0) {
+      for (int g2 = 1; g2 < CC::PG; ++g2) {
+        const float4 t = sAcc[g2 * CC::OUT4 + tid];
+        acc[0].x += t.x;
+        acc[0].y += t.y;
+        acc[0].z += t.z;
+        acc[0].w += t.w;
+      }
+    }
+  }
+  if (pg == 0) {
+#pragma unroll
+    for (int i = 0; i < CC::OPT; ++i) {
+      const int o = (NTHR >= CC::OUT4) ? tid : tid + i * NTHR;
+      const int d = o / (GT / 4);
+      const int h0 = (o % (GT / 4)) * 4;
+      const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+      if (out_rows != nullptr) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int h = 4 * h4 + e;
-          w[h] = (!ok[u] || M[h] == neg_inf()) ? 0.f : ex2(a[e] - M[h]);
+          const int h = h0 + e;
+          if (h < hcnt) {
+            const float L = sL[h];
+            out_rows[(size_t)h * D + d] = __float2half_rn(L > 0.f ? a4[e] / L : 0.f);
+          }
         }
-      }
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        const int h = (4 * q) % GT;
-        acc[4 * q + 0] += w[h + 0] * v[u][q].x;
-        acc[4 * q + 1] += w[h + 1] * v[u][q].y;
-        acc[4 * q + 2] += w[h + 2] * v[u][q].z;
-        acc[4 * q + 3] += w[h + 3] * v[u][q].w;
+      } else {
+        reinterpret_cast<float4*>(out_slot)[o] = acc[i];
       }
     }
   }
-  if (out_rows != nullptr) {
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      if (h < hcnt) {
-        float inv = 0.f;
-        if (L[h] > 0.f) {
-          inv = 1.f / L[h];
-        } else if (lane == 0) {
-          flag_error(status, PA_ERR_EMPTY_CONTEXT);
-        }
-        __half tmp[DPL];
-#pragma unroll
-        for (int dd = 0; dd < DPL; ++dd) tmp[dd] = __float2half_rn(acc[dd * GT + h] * inv);
-        __half* dst = out_rows + (size_t)h * D + lane * DPL;
-        if constexpr (DPL == 4) {
-          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(tmp);
-        } else {
-#pragma unroll
-          for (int dd = 0; dd < DPL; ++dd) dst[dd] = tmp[dd];
-        }
-      }
-    }
-  } else {
-    float4* rows = reinterpret_cast<float4*>(out_slot + lane * DPL * GT);
-#pragma unroll
-    for (int q = 0; q < Q; ++q)
-      rows[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-    if (lane == 0) {
-#pragma unroll
-      for (int h = 0; h < GT; ++h) {
-        out_slot[D * GT + h] = M[h];
-        out_slot[D * GT + GT + h] = L[h];
-      }
+  if (tid < GT) {
+    if (out_slot != nullptr) {
+      out_slot[D * GT + tid] = sM[tid];
+      out_slot[D * GT + GT + tid] = sL[tid];
+    } else if (tid < hcnt && !(sL[tid] > 0.f)) {
+      flag_error(status, PA_ERR_EMPTY_CONTEXT);
     }
   }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -214,6 +258,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ int s_tmp[32];
   __shared__ int s_empty;
   __shared__ int s_pend[WARPS][2][6];
+  __shared__ int s_npend[WARPS];
   extern __shared__ __align__(16) uint8_t dsm_raw[];
 
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
@@ -345,15 +390,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // ---- 2. This warp's page range ------------------------------------------------------------
   const long long Wt = min((long long)a.total_warps, (long long)T);
   const int wg = blockIdx.x * WARPS + warp;
-  if (wg >= Wt) return;
-  long long p0 = (long long)wg * T / Wt;
-  long long p1 = (long long)(wg + 1) * T / Wt;
-  if (a.mode == kModeSplit) {
-    p0 = snap(p0);
-    p1 = snap(p1);
+  long long p0 = 0, p1 = 0;
+  if (wg < Wt) {
+    p0 = (long long)wg * T / Wt;
+    p1 = (long long)(wg + 1) * T / Wt;
+    if (a.mode == kModeSplit) {
+      p0 = snap(p0);
+      p1 = snap(p1);
+    }
   }
   const int n = (int)(p1 - p0);
-  if (n <= 0) return;
+  int npend = 0;  // segments whose merge this warp owes (it arrived last)
+  if (n > 0) {
 
   // ---- 3. Producer: block ids for 32 upcoming pages live one per lane -----------------------
   struct PB { int blk, kvh, sub; };
@@ -468,7 +516,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   float oacc[MT][NT][4];
 
   int jfail = -1;
-  int npend = 0;
   for (int j = 0; j < n; ++j) {
     const int s = j % DEPTH;
     const bool split = (a.mode == kModeSplit);
@@ -800,43 +847,54 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
 
-  // Deferred log-sum-exp merges of the segments this warp completed last.
-  __syncwarp();
-  for (int e = 0; e < npend; ++e) {
-    const int* pe = s_pend[warp][e];
-    const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
-    __threadfence();
-    auto piece = [&](int k) -> const float* {
-      return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
-    };
-    if (a.mode == kModeStream) {
-      combine_pieces<D, GT>(piece, np, lane, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
-                            nullptr, a.status);
-    } else {
-      combine_pieces<D, GT>(piece, np, lane, hcnt, nullptr, a.part_out + (size_t)segid * SLOT,
-                            a.status);
-    }
-    if (lane == 0) a.counters[segid] = 0;
-  }
-
   if (jfail >= 0) {
     // Let copies still in flight land before the CTA's shared memory is released.
     for (int j = jfail; j < issued; ++j) {
       (void)mbar_wait_bounded(&wbar[j % DEPTH], (uint32_t)(j / DEPTH) & 1u, nullptr);
     }
   }
+  }  // n > 0
+
+  // ---- 5. CTA-cooperative merges of the segments completed by this CTA's warps ---------------
+  if (lane == 0) s_npend[warp] = npend;
+  __syncthreads();  // every warp is past its page loop: the ring memory is free scratch
+  float* scratch = reinterpret_cast<float*>(k_tiles);
+  for (int w = 0; w < WARPS; ++w) {
+    for (int e = 0; e < s_npend[w]; ++e) {
+      const int* pe = s_pend[w][e];
+      const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
+      __threadfence();
+      if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) >
+          (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST)) {
+        if (threadIdx.x == 0) flag_error(a.status, PA_ERR_WORKSPACE);
+        continue;
+      }
+      auto piece = [&](int k) -> const float* {
+        return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
+      };
+      if (a.mode == kModeStream) {
+        coop_combine<D, GT, NTHR, 8>(piece, np, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
+                                     nullptr, a.status, scratch);
+      } else {
+        coop_combine<D, GT, NTHR, 8>(piece, np, hcnt, nullptr,
+                                     a.part_out + (size_t)segid * SLOT, a.status, scratch);
+      }
+      if (threadIdx.x == 0) a.counters[segid] = 0;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------
-// LSE reduce: one warp per (sequence, kv-head, head tile) segment.
+// LSE reduce of the split-K pair (and of partials gathered across GPUs): one CTA of
+// kReduceThreads threads per (sequence, kv-head, head tile) segment, merged cooperatively.
 // ---------------------------------------------------------------------------------------
+constexpr int kReduceThreads = 512;
+
 template <int D, int GT>
-__global__ void __launch_bounds__(128) reduce_kernel(const ReduceArgs a) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kReduceThreads, 1) reduce_kernel(const ReduceArgs a) {
+  extern __shared__ __align__(16) float rsm[];
   const int SEGS = a.KVH * a.HT;
-  const int segid = blockIdx.x * 4 + warp;
-  if (segid >= a.B * SEGS) return;
+  const int segid = blockIdx.x;
   const int b = segid / SEGS;
   const int seg = segid - b * SEGS;
   const int kvh = seg / a.HT;
@@ -853,13 +911,14 @@ __global__ void __launch_bounds__(128) reduce_kernel(const ReduceArgs a) {
   }
   __half* orow = a.out + ((size_t)b * a.H + hbase) * D;
   if (np == 0) {
-    for (int i = lane; i < hcnt * D; i += 32) orow[(i / D) * D + (i % D)] = __float2half_rn(0.f);
-    if (lane == 0 && seg == 0) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
+    for (int i = threadIdx.x; i < hcnt * D; i += blockDim.x) orow[i] = __float2half_rn(0.f);
+    if (threadIdx.x == 0 && seg == 0) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
     return;
   }
   const float* base = a.part + (size_t)segid * a.seg_stride;
-  combine_pieces<D, GT>([&](int k) { return base + (size_t)k * a.piece_stride; }, np, lane,
-                        hcnt, orow, nullptr, a.status);
+  coop_combine<D, GT, kReduceThreads, 16>(
+      [&](int k) { return base + (size_t)k * a.piece_stride; }, np, hcnt, orow, nullptr,
+      a.status, rsm);
 }
 
 // Launch shapes per (cache dtype, head tile): warps per CTA (one CTA per SM) and ring depth
@@ -922,14 +981,25 @@ cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensor
                  : launch_one<0, 16>(a, maps, grid, stream);
 }
 
-cudaError_t launch_reduce(int gt, const ReduceArgs& a, cudaStream_t stream) {
+cudaError_t launch_reduce(int gt, const ReduceArgs& a, int max_pieces, cudaStream_t stream) {
   const int segs = a.B * a.KVH * a.HT;
-  const int grid = (segs + 3) / 4;
-  if (grid == 0) return cudaSuccess;
+  if (segs == 0) return cudaSuccess;
+  size_t smem;
+  cudaError_t e;
+  if (Coop<128, 16, kReduceThreads, 16>::floats(max_pieces) * sizeof(float) > 200 * 1024)
+    return cudaErrorInvalidValue;  // more splits than one CTA can merge (contexts > ~3M tokens)
   if (gt == 8) {
-    reduce_kernel<128, 8><<<grid, 128, 0, stream>>>(a);
+    smem = Coop<128, 8, kReduceThreads, 16>::floats(max_pieces) * sizeof(float);
+    e = cudaFuncSetAttribute(reduce_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    reduce_kernel<128, 8><<<segs, kReduceThreads, smem, stream>>>(a);
   } else {
-    reduce_kernel<128, 16><<<grid, 128, 0, stream>>>(a);
+    smem = Coop<128, 16, kReduceThreads, 16>::floats(max_pieces) * sizeof(float);
+    e = cudaFuncSetAttribute(reduce_kernel<128, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    reduce_kernel<128, 16><<<segs, kReduceThreads, smem, stream>>>(a);
   }
   return cudaGetLastError();
 }

@@ -61,7 +61,7 @@ struct ReduceArgs {
 // Launch helpers implemented in decode.cu. They return a cudaError_t.
 cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensorMap* maps,
                           int grid, cudaStream_t stream);
-cudaError_t launch_reduce(int gt, const ReduceArgs& a, cudaStream_t stream);
+cudaError_t launch_reduce(int gt, const ReduceArgs& a, int max_pieces, cudaStream_t stream);
 int decode_warps_per_cta(int kv_i8, int gt);
 cudaError_t launch_write_rows(int in_dtype, bool i8, int D, const void* k, const void* v,
                               long long token_stride, const int* slots, int N, int KVH,
