@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   PB cur = batch_info(0);
   PB nxt = batch_info(32);
 
-  auto issue = [&](int j) {
+  auto issue = [&](int j, int s) {
     if (j > 0 && (j & 31) == 0) {
       cur = nxt;
       nxt = batch_info(j + 32);
@@ -436,7 +436,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         blk = 0;
       }
       const int row = blk * a.KVH + kvh;
-      const int s = j % DEPTH;
       uint64_t* bar = &wbar[s];
       uint8_t* kd = k_tiles + (warp * DEPTH + s) * C::KT;
       uint8_t* vd = v_tiles + (warp * DEPTH + s) * C::VT;
@@ -466,58 +465,127 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   const int npro = n < DEPTH ? n : DEPTH;
   __syncwarp();
-  for (int j = 0; j < npro; ++j) issue(j);
+  for (int j = 0; j < npro; ++j) issue(j, j);
   int issued = npro;
 
   // ---- 4. Consumer state ---------------------------------------------------------------------
   int cb, cseg, csp;
   locate((int)p0, cb, cseg, csp);
   int cpg = pages_of(cb);
+  int cctx = s_ctx[cb];
   int piece_sp0 = csp;
   const float qs = a.qk_scale_log2;
 
+  // Q fragments. FP16 cache: fp16 A fragments of the m16n8k16 MMA (qa rows g, qb rows g+8).
+  // INT8 cache: each q row is split into two int8 parts, q ~ qsc * (q1 + q2 / 254) (error at
+  // most qsc / 508 per element), held as A fragments of the integer m16n8k32 MMA, so raw K
+  // bytes feed the tensor cores with no unpacking: x = {q1 lo, q1 hi, q2 lo, q2 hi}.
   uint4 qa[NS], qb[NS];
+  float qsc0 = 0.f, qsc1 = 0.f;
   int q_b = -1, q_seg = -1;
+
+  auto split_row = [&](const uint4 (&src)[NS], uint4 (&dst)[NS], float& qsc) {
+    float amax = 0.f;
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    qsc = amax * (1.f / 127.f);
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
+      int q1[8], q2[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+        const float t0 = f.x * inv, t1 = f.y * inv;
+        const int a0 = max(-127, min(127, __float2int_rn(t0)));
+        const int a1 = max(-127, min(127, __float2int_rn(t1)));
+        q1[2 * e] = a0;
+        q1[2 * e + 1] = a1;
+        q2[2 * e] = max(-127, min(127, __float2int_rn((t0 - (float)a0) * 254.f)));
+        q2[2 * e + 1] = max(-127, min(127, __float2int_rn((t1 - (float)a1) * 254.f)));
+      }
+      dst[si] = make_uint4(pack_s8x4(q1[0], q1[1], q1[2], q1[3]),
+                           pack_s8x4(q1[4], q1[5], q1[6], q1[7]),
+                           pack_s8x4(q2[0], q2[1], q2[2], q2[3]),
+                           pack_s8x4(q2[4], q2[5], q2[6], q2[7]));
+    }
+  };
 
   auto load_q = [&](int b, int seg) {
     const int kvh = seg / a.HT;
     const int ht = seg - kvh * a.HT;
     const int hl = ht * GT + g;
     const __half* qrow = a.q + ((size_t)b * a.H + (size_t)kvh * a.G + hl) * D;
+    uint4 ra[NS], rb[NS];
 #pragma unroll
     for (int si = 0; si < NS; ++si) {
       const int c = I8 ? chunk_i8(r, si) : chunk_f16(r, si);
-      qa[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
+      ra[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
                           : make_uint4(0u, 0u, 0u, 0u);
       if constexpr (GT == 16) {
-        qb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
+        rb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
                                 : make_uint4(0u, 0u, 0u, 0u);
       } else {
-        qb[si] = make_uint4(0u, 0u, 0u, 0u);
+        rb[si] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    if constexpr (I8) {
+      split_row(ra, qa, qsc0);
+      if constexpr (GT == 16) {
+        split_row(rb, qb, qsc1);
+      } else {
+#pragma unroll
+        for (int si = 0; si < NS; ++si) qb[si] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else {
+#pragma unroll
+      for (int si = 0; si < NS; ++si) {
+        qa[si] = ra[si];
+        qb[si] = rb[si];
       }
     }
   };
 
-  // Shared-memory offset of the K cell (chunk of load si, token of n-tile jt) this lane reads.
-  auto koff = [&](int si, int jt) -> uint32_t {
-    const int tau = 4 * (g >> 1) + (g & 1) + 2 * jt;
-    if constexpr (I8) {
-      const int c = chunk_i8(r, si);
-      return c * 128 + ((((tau >> 1) ^ (c & 7)) << 4) | ((tau & 1) << 3));
-    } else {
-      const int c = chunk_f16(r, si);
-      const int row = 2 * c + (tau >> 3);
-      return row * 128 + (((tau & 7) ^ (row & 7)) << 4);
+  // Shared-memory offsets of the K cells this lane reads (chunk of load si, token of n-tile
+  // jt), fixed for the whole kernel.
+  uint32_t koff[NS][2];
+#pragma unroll
+  for (int si = 0; si < NS; ++si) {
+#pragma unroll
+    for (int jt = 0; jt < 2; ++jt) {
+      const int tau = 4 * (g >> 1) + (g & 1) + 2 * jt;
+      if constexpr (I8) {
+        const int c = chunk_i8(r, si);
+        koff[si][jt] = c * 128 + ((((tau >> 1) ^ (c & 7)) << 4) | ((tau & 1) << 3));
+      } else {
+        const int c = chunk_f16(r, si);
+        const int row = 2 * c + (tau >> 3);
+        koff[si][jt] = row * 128 + (((tau & 7) ^ (row & 7)) << 4);
+      }
     }
-  };
+  }
   const uint32_t voff = I8 ? (uint32_t)(g * 16 + 4 * r) : (uint32_t)((g * 16 + 4 * r) * 2);
+  const uint32_t kbase = smem_u32(k_tiles) + warp * DEPTH * C::KT;
+  const uint32_t vbase = smem_u32(v_tiles) + warp * DEPTH * C::VT;
+  const uint32_t sbase = I8 ? smem_u32(s_tiles) + warp * DEPTH * C::ST : 0u;
 
   float m0 = neg_inf(), l0 = 0.f, m1 = neg_inf(), l1 = 0.f;
   float oacc[MT][NT][4];
 
   int jfail = -1;
+  int s = 0;        // ring stage of page j
+  uint32_t ph = 0;  // its mbarrier phase parity
   for (int j = 0; j < n; ++j) {
-    const int s = j % DEPTH;
     const bool split = (a.mode == kModeSplit);
     const bool first = (j == 0) || (split ? (csp % kSplitPages == 0) : (csp == 0));
     const bool last = (j == n - 1) || (csp == cpg - 1) ||
@@ -541,17 +609,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       piece_sp0 = csp;
     }
 
-    if (!mbar_wait_bounded(&wbar[s], (uint32_t)(j / DEPTH) & 1u, a.status)) {
+    if (!mbar_wait_bounded(&wbar[s], ph, a.status)) {
       jfail = j;
       break;
     }
 
     // ---- stage -> registers, then hand the stage back to the TMA right away -------------------
-    const int valid = min(kSubTokens, s_ctx[cb] - csp * kSubTokens);
-    const uint32_t kb = smem_u32(k_tiles + (warp * DEPTH + s) * C::KT);
-    const uint32_t vb = smem_u32(v_tiles + (warp * DEPTH + s) * C::VT);
-    const uint32_t sb = I8 ? smem_u32(s_tiles + (warp * DEPTH + s) * C::ST) : 0u;
-    // K: INT8 8 bytes per (si, jt) cell; FP16 16 bytes.
+    const int valid = min(kSubTokens, cctx - csp * kSubTokens);
+    const uint32_t kb = kbase + s * C::KT;
+    const uint32_t vb = vbase + s * C::VT;
+    const uint32_t sb = sbase + s * C::ST;
     uint2 k8[NS][2];
     uint4 k16[NS][2];
     uint32_t v8[MT][2];
@@ -561,8 +628,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     for (int si = 0; si < NS; ++si) {
 #pragma unroll
       for (int jt = 0; jt < 2; ++jt) {
-        if constexpr (I8) k8[si][jt] = lds64(kb + koff(si, jt));
-        else k16[si][jt] = lds128(kb + koff(si, jt));
+        if constexpr (I8) k8[si][jt] = lds64(kb + koff[si][jt]);
+        else k16[si][jt] = lds128(kb + koff[si][jt]);
       }
     }
 #pragma unroll
@@ -582,46 +649,77 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __syncwarp();
     if (j + DEPTH < n) {
       if (lane == 0) fence_proxy_async_smem();
-      issue(j + DEPTH);
+      issue(j + DEPTH, s);
       ++issued;
     }
 
     // ---- one 16-token subpage from registers ---------------------------------------------------
     {
-      // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n). Two accumulation
-      // chains per n-tile (even / odd si) shorten the dependent MMA sequence.
-      float sacc[2][2][4];
+      // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n); tokens 4r..4r+3 of
+      // head g end up in x[0..3] (and of head g+8 in y[0..3]).
+      float x[4], y[4];
+      if constexpr (I8) {
+        int sa[2][4], sbq[2][4];
 #pragma unroll
-      for (int jt = 0; jt < 2; ++jt)
+        for (int jt = 0; jt < 2; ++jt)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sacc[jt][hh][e] = 0.f;
-#pragma unroll
-      for (int si = 0; si < NS; ++si) {
-#pragma unroll
-        for (int jt = 0; jt < 2; ++jt) {
-          uint32_t b0a, b1a, b0b, b1b;
-          if constexpr (I8) {
-            i8x4_to_f16x2x2(k8[si][jt].x, b0a, b1a);
-            i8x4_to_f16x2x2(k8[si][jt].y, b0b, b1b);
-          } else {
-            b0a = k16[si][jt].x;
-            b1a = k16[si][jt].y;
-            b0b = k16[si][jt].z;
-            b1b = k16[si][jt].w;
+          for (int e = 0; e < 4; ++e) {
+            sa[jt][e] = 0;
+            sbq[jt][e] = 0;
           }
-          float (&acc)[4] = sacc[jt][si & 1];
-          mma_16816(acc, qa[si].x, qb[si].x, qa[si].y, qb[si].y, b0a, b1a);
-          mma_16816(acc, qa[si].z, qb[si].z, qa[si].w, qb[si].w, b0b, b1b);
+#pragma unroll
+        for (int si = 0; si < NS; ++si) {
+#pragma unroll
+          for (int jt = 0; jt < 2; ++jt) {
+            imma_16832(sa[jt], qa[si].x, qb[si].x, qa[si].y, qb[si].y, k8[si][jt].x,
+                       k8[si][jt].y);
+            imma_16832(sbq[jt], qa[si].z, qb[si].z, qa[si].w, qb[si].w, k8[si][jt].x,
+                       k8[si][jt].y);
+          }
         }
+        constexpr float kLo = 1.f / 254.f;
+        x[0] = fmaf((float)sbq[0][0], kLo, (float)sa[0][0]) * qsc0;
+        x[1] = fmaf((float)sbq[0][1], kLo, (float)sa[0][1]) * qsc0;
+        x[2] = fmaf((float)sbq[1][0], kLo, (float)sa[1][0]) * qsc0;
+        x[3] = fmaf((float)sbq[1][1], kLo, (float)sa[1][1]) * qsc0;
+        if constexpr (NT == 2) {
+          y[0] = fmaf((float)sbq[0][2], kLo, (float)sa[0][2]) * qsc1;
+          y[1] = fmaf((float)sbq[0][3], kLo, (float)sa[0][3]) * qsc1;
+          y[2] = fmaf((float)sbq[1][2], kLo, (float)sa[1][2]) * qsc1;
+          y[3] = fmaf((float)sbq[1][3], kLo, (float)sa[1][3]) * qsc1;
+        } else {
+          y[0] = y[1] = y[2] = y[3] = 0.f;
+        }
+      } else {
+        // Two accumulation chains per n-tile (even / odd si) shorten the MMA dependency.
+        float sacc[2][2][4];
+#pragma unroll
+        for (int jt = 0; jt < 2; ++jt)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sacc[jt][hh][e] = 0.f;
+#pragma unroll
+        for (int si = 0; si < NS; ++si) {
+#pragma unroll
+          for (int jt = 0; jt < 2; ++jt) {
+            float (&acc)[4] = sacc[jt][si & 1];
+            mma_16816(acc, qa[si].x, qb[si].x, qa[si].y, qb[si].y, k16[si][jt].x,
+                      k16[si][jt].y);
+            mma_16816(acc, qa[si].z, qb[si].z, qa[si].w, qb[si].w, k16[si][jt].z,
+                      k16[si][jt].w);
+          }
+        }
+        x[0] = sacc[0][0][0] + sacc[0][1][0];
+        x[1] = sacc[0][0][1] + sacc[0][1][1];
+        x[2] = sacc[1][0][0] + sacc[1][1][0];
+        x[3] = sacc[1][0][1] + sacc[1][1][1];
+        y[0] = sacc[0][0][2] + sacc[0][1][2];
+        y[1] = sacc[0][0][3] + sacc[0][1][3];
+        y[2] = sacc[1][0][2] + sacc[1][1][2];
+        y[3] = sacc[1][0][3] + sacc[1][1][3];
       }
-
-      // Scores of tokens 4r..4r+3 for heads g (x) and g+8 (y), in log2 units.
-      float x[4] = {sacc[0][0][0] + sacc[0][1][0], sacc[0][0][1] + sacc[0][1][1],
-                    sacc[1][0][0] + sacc[1][1][0], sacc[1][0][1] + sacc[1][1][1]};
-      float y[4] = {sacc[0][0][2] + sacc[0][1][2], sacc[0][0][3] + sacc[0][1][3],
-                    sacc[1][0][2] + sacc[1][1][2], sacc[1][0][3] + sacc[1][1][3]};
+      // Logits in log2 units.
       float ksc[4] = {qs, qs, qs, qs};
       if constexpr (I8) {
         ksc[0] = ksv.x * qs;
@@ -697,11 +795,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
       if constexpr (I8) {
         const float vsc[4] = {vsv.x, vsv.y, vsv.z, vsv.w};
+        if (valid < kSubTokens) {
+          // Scales of slots past the context may hold anything: keep them out of P'.
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const bool ok = (4 * r + e) < valid;
-          pv[e] = ok ? p[e] * vsc[e] : 0.f;
-          if constexpr (NT == 2) py[e] = ok ? py[e] * vsc[e] : 0.f;
+          for (int e = 0; e < 4; ++e) {
+            const bool ok = (4 * r + e) < valid;
+            pv[e] = ok ? p[e] * vsc[e] : 0.f;
+            if constexpr (NT == 2) py[e] = ok ? py[e] * vsc[e] : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            pv[e] = p[e] * vsc[e];
+            if constexpr (NT == 2) py[e] *= vsc[e];
+          }
         }
       }
       const uint32_t pb0 = pack_f16x2(pv[0], pv[1]);
@@ -834,16 +941,21 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
 
-    // Advance the consumer iterator.
+    // Advance the consumer iterator and the ring stage.
     if (++csp == cpg) {
       csp = 0;
       if (++cseg == SEGS) {
         cseg = 0;
         if (j + 1 < n) {
           do { ++cb; } while (pages_of(cb) == 0);
+          cctx = s_ctx[cb];
         }
       }
       if (j + 1 < n) cpg = pages_of(cb);
+    }
+    if (++s == DEPTH) {
+      s = 0;
+      ph ^= 1u;
     }
   }
 
