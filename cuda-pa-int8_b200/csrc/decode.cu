@@ -67,6 +67,108 @@ struct Tile {
 };
 
 // ---------------------------------------------------------------------------------------
+// Warp-level log-sum-exp merge for segments with few pieces (np <= 32): lane k reads piece
+// k's maxima and denominators; the O rows are then accumulated two pieces per step, each
+// lane owning head_dim rows [lane*D/32, (lane+1)*D/32). Several of these run in parallel,
+// one per warp.
+// ---------------------------------------------------------------------------------------
+constexpr int kWarpMergeMax = 32;
+
+template <int D, int GT, typename PieceFn>
+__device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, int hcnt,
+                                             __half* out_rows, float* out_slot, int* status) {
+  constexpr int DPL = D / 32;
+  constexpr int Q = DPL * GT / 4;
+  float mk[GT], lk[GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) {
+    mk[h] = neg_inf();
+    lk[h] = 0.f;
+  }
+  if (lane < np) {
+    const float4* sl = reinterpret_cast<const float4*>(piece(lane) + D * GT);
+#pragma unroll
+    for (int h4 = 0; h4 < GT / 4; ++h4) {
+      const float4 m4 = __ldcg(sl + h4);
+      const float4 l4 = __ldcg(sl + GT / 4 + h4);
+      mk[4 * h4 + 0] = m4.x; mk[4 * h4 + 1] = m4.y; mk[4 * h4 + 2] = m4.z; mk[4 * h4 + 3] = m4.w;
+      lk[4 * h4 + 0] = l4.x; lk[4 * h4 + 1] = l4.y; lk[4 * h4 + 2] = l4.z; lk[4 * h4 + 3] = l4.w;
+    }
+  }
+  float wk[GT], L[GT], M[GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) {
+    M[h] = warp_max(mk[h]);
+    wk[h] = (M[h] == neg_inf() || lane >= np) ? 0.f : ex2(mk[h] - M[h]);
+    float v = wk[h] * lk[h];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    L[h] = v;
+  }
+  float acc[DPL * GT];
+#pragma unroll
+  for (int i = 0; i < DPL * GT; ++i) acc[i] = 0.f;
+  for (int k = 0; k < np; k += 2) {
+    const bool two = (k + 1) < np;
+    float4 v0[Q], v1[Q];
+    const float4* r0 = reinterpret_cast<const float4*>(piece(k) + lane * DPL * GT);
+    const float4* r1 = reinterpret_cast<const float4*>(piece(two ? k + 1 : k) + lane * DPL * GT);
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      v0[q] = __ldcg(r0 + q);
+      v1[q] = __ldcg(r1 + q);
+    }
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const int h = (4 * q) % GT;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float w0 = __shfl_sync(0xffffffffu, wk[h + e], k);
+        const float w1 = two ? __shfl_sync(0xffffffffu, wk[h + e], k + 1) : 0.f;
+        const float a0 = e == 0 ? v0[q].x : e == 1 ? v0[q].y : e == 2 ? v0[q].z : v0[q].w;
+        const float a1 = e == 0 ? v1[q].x : e == 1 ? v1[q].y : e == 2 ? v1[q].z : v1[q].w;
+        acc[4 * q + e] += w0 * a0 + w1 * a1;
+      }
+    }
+  }
+  if (out_rows != nullptr) {
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+      if (h < hcnt) {
+        float inv = 0.f;
+        if (L[h] > 0.f) {
+          inv = 1.f / L[h];
+        } else if (lane == 0) {
+          flag_error(status, PA_ERR_EMPTY_CONTEXT);
+        }
+        __half tmp[DPL];
+#pragma unroll
+        for (int dd = 0; dd < DPL; ++dd) tmp[dd] = __float2half_rn(acc[dd * GT + h] * inv);
+        __half* dst = out_rows + (size_t)h * D + lane * DPL;
+        if constexpr (DPL == 4) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(tmp);
+        } else {
+#pragma unroll
+          for (int dd = 0; dd < DPL; ++dd) dst[dd] = tmp[dd];
+        }
+      }
+    }
+  } else {
+    float4* rows = reinterpret_cast<float4*>(out_slot + lane * DPL * GT);
+#pragma unroll
+    for (int q = 0; q < Q; ++q)
+      rows[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+    if (lane == 0) {
+#pragma unroll
+      for (int h = 0; h < GT; ++h) {
+        out_slot[D * GT + h] = M[h];
+        out_slot[D * GT + GT + h] = L[h];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
 // CTA-cooperative log-sum-exp merge of `np` partial slots (all NTHR threads of the block take
 // part; scratch is shared memory). Pass 1 forms the maxima, the per-piece weights (kept in
 // shared memory) and the denominators with every thread reading a different piece; pass 2
@@ -967,14 +1069,41 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   }  // n > 0
 
-  // ---- 5. CTA-cooperative merges of the segments completed by this CTA's warps ---------------
+  // ---- 5. Merges of the segments whose last piece this CTA's warps finished ------------------
+  // Segments with few pieces are merged one per warp, in parallel; larger ones by the whole
+  // CTA together.
   if (lane == 0) s_npend[warp] = npend;
   __syncthreads();  // every warp is past its page loop: the ring memory is free scratch
   float* scratch = reinterpret_cast<float*>(k_tiles);
+  // 16-row head tiles keep more registers per piece: those always merge cooperatively.
+  constexpr int kWarpMerge = (GT == 8) ? kWarpMergeMax : 0;
+  int idx = 0;
+  for (int w = 0; w < WARPS; ++w) {
+    for (int e = 0; e < s_npend[w]; ++e) {
+      const int* pe = s_pend[w][e];
+      const int np = pe[2];
+      if (np > kWarpMerge) continue;
+      if ((idx++ % WARPS) != warp) continue;
+      const int segid = pe[0], wf = pe[1], b = pe[3], hbase = pe[4], hcnt = pe[5];
+      __threadfence();
+      auto piece = [&](int k) -> const float* {
+        return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
+      };
+      if (a.mode == kModeStream) {
+        warp_combine<D, GT>(piece, np, lane, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
+                            nullptr, a.status);
+      } else {
+        warp_combine<D, GT>(piece, np, lane, hcnt, nullptr, a.part_out + (size_t)segid * SLOT,
+                            a.status);
+      }
+      if (lane == 0) a.counters[segid] = 0;
+    }
+  }
   for (int w = 0; w < WARPS; ++w) {
     for (int e = 0; e < s_npend[w]; ++e) {
       const int* pe = s_pend[w][e];
       const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
+      if (np <= kWarpMerge) continue;
       __threadfence();
       if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) >
           (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST)) {
