@@ -1075,8 +1075,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   if (lane == 0) s_npend[warp] = npend;
   __syncthreads();  // every warp is past its page loop: the ring memory is free scratch
   float* scratch = reinterpret_cast<float*>(k_tiles);
-  // 16-row head tiles keep more registers per piece: those always merge cooperatively.
-  constexpr int kWarpMerge = (GT == 8) ? kWarpMergeMax : 0;
+  // A CTA with many merges runs them one per warp in parallel; one with a few merges runs the
+  // larger of them cooperatively (all warps on one merge). 16-row head tiles keep more
+  // registers per piece and always merge cooperatively.
+  int n_merges = 0;
+  for (int w = 0; w < WARPS; ++w) n_merges += s_npend[w];
+  const int kWarpMerge =
+      (GT != 8) ? 0 : (n_merges * 4 >= WARPS ? kWarpMergeMax : 4);
   int idx = 0;
   for (int w = 0; w < WARPS; ++w) {
     for (int e = 0; e < s_npend[w]; ++e) {
