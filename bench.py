@@ -244,52 +244,57 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 # CPU baseline: the oracle port of the reference decode on a bounded sample
 # ---------------------------------------------------------------------------------------
-def cpu_baseline(cfg, budget_s=10.0):
+def _cpu_sample(cfg):
+    """One bounded CPU step of the workload: the decode of one sequence (at most 8192
+    tokens) of the configuration's shape, through the oracle port of the reference algorithm
+    (tests/paged_decode_attn.py:4-49; INT8 via dequantize_kv first, :202-216)."""
     import numpy as np
     sys.path.insert(0, os.path.join(HERE, "oracle"))
     import pa_oracle
-    if cfg == 2:
-        H, KVH, ctx, int8 = 32, 8, 4096, False
-    elif cfg == 3:
-        H, KVH, ctx, int8 = 12, 2, 8192, True
-    elif cfg == 4:
-        H, KVH, ctx, int8 = 64, 8, 98304, True
-    else:
-        H, KVH, ctx, int8 = 28, 4, 3000, True
-    S = 2
+    H, KVH, ctx, int8 = {2: (32, 8, 4096, False), 3: (12, 2, 8192, True),
+                         4: (64, 8, 8192, True), 5: (28, 4, 3376, True)}[cfg]
     nblk = (ctx + BLOCK - 1) // BLOCK
     rng = np.random.default_rng(7)
-    bt = rng.permutation(S * nblk).reshape(S, nblk).astype(np.int32)
-    lens = np.full(S, ctx, np.int32)
-    q = rng.standard_normal((S, H, HEAD_DIM), dtype=np.float32).astype(np.float16)
+    bt = rng.permutation(nblk).reshape(1, nblk).astype(np.int32)
+    lens = np.full(1, ctx, np.int32)
+    q = rng.standard_normal((1, H, HEAD_DIM), dtype=np.float32).astype(np.float16)
     if int8:
-        kc = rng.integers(-127, 128, (S * nblk, KVH, 16, BLOCK, 8), dtype=np.int8)
-        vc = rng.integers(-127, 128, (S * nblk, KVH, HEAD_DIM, BLOCK), dtype=np.int8)
-        ks = rng.random((S * nblk, KVH, BLOCK), dtype=np.float32) * 0.05
-        vs = rng.random((S * nblk, KVH, BLOCK), dtype=np.float32) * 0.05
-    else:
-        kc = rng.standard_normal((S * nblk, KVH, 16, BLOCK, 8), dtype=np.float32).astype(np.float16)
-        vc = rng.standard_normal((S * nblk, KVH, HEAD_DIM, BLOCK), dtype=np.float32).astype(np.float16)
-    per_tok = KVH * (2 * HEAD_DIM * (1 if int8 else 2) + (8 if int8 else 0))
-    done_bytes = 0
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        if int8:
+        kc = rng.integers(-127, 128, (nblk, KVH, 16, BLOCK, 8), dtype=np.int8)
+        vc = rng.integers(-127, 128, (nblk, KVH, HEAD_DIM, BLOCK), dtype=np.int8)
+        ks = rng.random((nblk, KVH, BLOCK), dtype=np.float32) * 0.05
+        vs = rng.random((nblk, KVH, BLOCK), dtype=np.float32) * 0.05
+
+        def step():
             kd, vd = pa_oracle.dequantize_kv(kc, vc, ks, vs)
             pa_oracle.paged_decode_attention(q, kd, vd, bt, lens, acc=np.float32)
-        else:
+    else:
+        kc = rng.standard_normal((nblk, KVH, 16, BLOCK, 8), dtype=np.float32).astype(np.float16)
+        vc = rng.standard_normal((nblk, KVH, HEAD_DIM, BLOCK), dtype=np.float32).astype(np.float16)
+
+        def step():
             pa_oracle.paged_decode_attention(q, kc, vc, bt, lens, acc=np.float32)
-        done_bytes += S * ctx * per_tok
-        reps += 1
+    per_tok = KVH * (2 * HEAD_DIM * (1 if int8 else 2) + (8 if int8 else 0))
+    desc = (f"1 sequence of ctx {ctx} ({H}/{KVH} heads{', int8 dequant' if int8 else ''}) per "
+            "step, numpy oracle decode (BLAS matmuls on all host threads)")
+    return step, ctx * per_tok, desc
+
+
+def cpu_baseline(cfg, steps=None, warmup=1, budget_s=10.0):
+    """Time the CPU reference path: `warmup` untimed steps, then `steps` timed steps (or as
+    many as fit in budget_s when steps is None). Returns the cpu_baseline record."""
+    step, nbytes, desc = _cpu_sample(cfg)
+    for _ in range(max(1, warmup)):
+        step()
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        step()
+        done += 1
         el = time.perf_counter() - t0
-        if el >= budget_s:
+        if (steps is not None and done >= steps) or (steps is None and el >= budget_s):
             break
-    cores = os.cpu_count() or 1
-    return {"value": done_bytes / el / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{reps} x {S} sequences of ctx {ctx} ({H}/{KVH} heads, "
-                      f"{'int8 dequant + ' if int8 else ''}numpy oracle decode), "
-                      f"{el:.1f} s"}
+    return {"value": done * nbytes / el / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1,
+            "kind": "port", "sample": f"{desc}; {done} steps in {el:.1f} s"}
 
 
 def profile_traffic(cfg):
@@ -330,7 +335,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        base = cpu_baseline(args.config)
+        base = cpu_baseline(args.config, steps=args.steps, warmup=args.warmup)
         line = {"metric": METRIC, "value": base["value"], "unit": "GB/s", "impl": "reference",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

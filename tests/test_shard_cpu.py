@@ -1,0 +1,114 @@
+"""CPU: multi-GPU sharding logic (pa_b200.shard) and the cross-rank split-context exchange,
+run as world-size-2 gloo process groups with the oracle standing in for the GPU kernels."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import gen
+import pa_oracle
+from pa_b200 import shard
+
+
+def test_lpt_partition_covers_and_balances():
+    rng = np.random.default_rng(0)
+    for world in (1, 2, 3, 4, 8):
+        lens = rng.integers(1, 5000, size=97).tolist()
+        parts = shard.lpt_partition(lens, world)
+        flat = sorted(i for p in parts for i in p)
+        assert flat == list(range(len(lens)))
+        loads = [sum(lens[i] for i in p) for p in parts]
+        # LPT bound: max load <= 4/3 * optimum <= 4/3 * max(mean, largest item)
+        lower = max(sum(lens) / world, max(lens))
+        assert max(loads) <= 4 / 3 * lower + 1e-9
+
+
+def test_lpt_partition_deterministic():
+    lens = [5, 5, 5, 5, 3, 3]
+    assert shard.lpt_partition(lens, 2) == shard.lpt_partition(lens, 2)
+
+
+def test_kv_head_slice():
+    q_heads, kv_heads = set(), set()
+    for r in range(4):
+        qs, ks = shard.kv_head_slice(64, 8, 4, r)
+        q_heads |= set(qs)
+        kv_heads |= set(ks)
+        assert len(qs) == 16 and len(ks) == 2
+        assert all(h // 8 in ks for h in qs)  # q head h belongs to kv head h // 8
+    assert q_heads == set(range(64)) and kv_heads == set(range(8))
+    with pytest.raises(ValueError):
+        shard.kv_head_slice(12, 2, 4, 0)
+
+
+@pytest.mark.parametrize("ctx", [1, 15, 16, 17, 100, 4096])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_token_ranges_are_block_aligned_and_cover(ctx, world):
+    rs = shard.token_ranges(ctx, world)
+    assert rs[0][0] == 0 and rs[-1][1] == ctx
+    for (a, b), (c, d) in zip(rs, rs[1:]):
+        assert b == c
+    for a, b in rs:
+        assert a % 16 == 0 and a <= b
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _split_context_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lens = [700, 33, 1, 1500]
+        c = gen.decode_case(seed=41, num_seqs=4, num_heads=8, num_kv_heads=2, context_lens=lens)
+        kc, vc = pa_oracle.scatter_paged_cache(c["k"], c["v"], c["context_lens"],
+                                               c["block_table"], c["num_blocks"])
+        scale = 1 / np.sqrt(128)
+        # This rank's share: block ids and context length of its token range per sequence.
+        S = len(lens)
+        bt_local = np.zeros_like(c["block_table"])
+        cl_local = np.zeros(S, np.int32)
+        for b in range(S):
+            blocks, n = shard.local_view(c["block_table"][b], lens[b], world, rank)
+            bt_local[b, :len(blocks)] = blocks
+            cl_local[b] = n
+        m, l, acc = pa_oracle.range_partials(c["q"], kc, vc, bt_local, cl_local,
+                                             np.zeros(S, np.int32), cl_local, scale)
+        local = torch.from_numpy(np.concatenate([m.ravel(), l.ravel(), acc.ravel()]))
+        gathered = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(gathered, local)
+        H, D = 8, 128
+        ms = np.stack([g[:S * H].numpy().reshape(S, H) for g in gathered])
+        ls = np.stack([g[S * H:2 * S * H].numpy().reshape(S, H) for g in gathered])
+        accs = np.stack([g[2 * S * H:].numpy().reshape(S, H, D) for g in gathered])
+        merged = pa_oracle.lse_merge(ms, ls, accs)
+        full = pa_oracle.paged_decode_attention(c["q"], kc, vc, c["block_table"],
+                                                c["context_lens"], scale=scale)
+        result_q.put((rank, float(np.abs(merged - full).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_context_exchange_gloo_world2():
+    """Two ranks each own a block-aligned half of every sequence; their partials, exchanged
+    with all_gather and LSE-merged, equal the one-pass decode."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_context_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=5) for _ in range(2))
+    assert all(err < 1e-5 for _, err in res), res
