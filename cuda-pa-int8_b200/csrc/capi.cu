@@ -353,6 +353,18 @@ int elem_size(int dt) { return dt == PA_DTYPE_F32 ? 4 : (dt == PA_DTYPE_I8 ? 1 :
 
 }  // namespace
 
+namespace pa {
+int fail_status(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+}  // namespace pa
+
 extern "C" {
 
 int pa_version(void) { return 100; }

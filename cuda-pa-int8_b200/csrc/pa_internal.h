@@ -76,6 +76,9 @@ cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float*
                                 int semantics, unsigned int* scratch, int num_sms,
                                 cudaStream_t st);
 
+// Record a message for pa_last_error() and return `code` (defined in capi.cu).
+int fail_status(int code, const char* fmt, ...);
+
 // Partial slot size in floats: O[D][GT] + m[GT] + l[GT].
 inline int slot_floats(int head_dim, int gt) { return (head_dim + 2) * gt; }
 

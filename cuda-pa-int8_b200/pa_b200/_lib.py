@@ -50,6 +50,8 @@ SIGNATURES = {
                           _vp, _sz, _vp]),
     "pa_splitk_f16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp,
                            _sz, _vp]),
+    "pa_decode_f16_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
+                                   _vp]),
     "pa_splitk_i8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
                           _vp, _sz, _vp]),
     "pa_partial_floats": (_i, [_i, _i, _i]),

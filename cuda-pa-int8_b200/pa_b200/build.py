@@ -18,7 +18,7 @@ INCLUDE_DIR = os.path.join(REPO_DIR, "include")
 LIB_NAME = "libpa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
-SOURCES = ["decode.cu", "quant.cu", "capi.cu"]
+SOURCES = ["decode.cu", "quant.cu", "capi.cu", "noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
     "-O3", "-lineinfo", "-std=c++17",

@@ -116,6 +116,19 @@ int pa_splitk_i8(void* out, const void* q, const void* k_cache, const void* v_ca
                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                  float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* FP16 single-pass decode that allocates nothing and takes no workspace, for callers that
+ * cannot allocate device memory when they run attention: plugins whose host framework owns
+ * all device memory, and serving loops that must stay out of any allocator. Its scratch is a
+ * 12 MiB static device array that every GPU loading this code keeps until the process exits;
+ * shapes whose scratch exceeds it (more than 8 q heads per kv head) are rejected with
+ * PA_ERR_WORKSPACE. The first call on a device looks up the array's address and should come
+ * before any stream capture. Calls share the array: calls that overlap on the GPU race, so
+ * order them on one stream. This entry point has no counterpart in the reference. */
+int pa_decode_f16_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
+                          const int32_t* block_table, const int32_t* context_lens, int num_seqs,
+                          int num_heads, int num_kv_heads, int head_dim, int num_blocks,
+                          int block_size, int max_blocks_per_seq, float scale, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Per-sequence partial decode for split-K across GPUs: like pa_decode_*, but instead of
  * the normalised fp16 output it writes, per (sequence, kv-head), an un-normalised partial
