@@ -89,7 +89,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA: 1-D bulk copies and tiled tensor copies, completing on an mbarrier (no multicast)
+// TMA: 1-D bulk copies and tiled tensor copies into this CTA's shared memory, completing on an mbarrier
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
