@@ -505,77 +505,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   int npend = 0;  // segments whose merge this warp owes (it arrived last)
   if (n > 0) {
 
-  // ---- 3. Producer: block ids for 32 upcoming pages live one per lane -----------------------
-  struct PB { int blk, kvh, sub; };
-  auto batch_info = [&](int jbase) {
-    PB o{0, 0, 0};
-    const int j = jbase + lane;
-    if (j < n) {
-      int b, seg, sp;
-      locate((int)(p0 + j), b, seg, sp);
-      o.kvh = seg / a.HT;
-      const int bi = sp / a.subs;
-      o.sub = sp - bi * a.subs;
-      o.blk = __ldg(a.block_table + (size_t)b * a.max_blocks + bi);
-    }
-    return o;
-  };
-  PB cur = batch_info(0);
-  PB nxt = batch_info(32);
-
-  auto issue = [&](int j, int s) {
-    if (j > 0 && (j & 31) == 0) {
-      cur = nxt;
-      nxt = batch_info(j + 32);
-    }
-    const int src = j & 31;
-    int blk = __shfl_sync(0xffffffffu, cur.blk, src);
-    const int kvh = __shfl_sync(0xffffffffu, cur.kvh, src);
-    const int sub = __shfl_sync(0xffffffffu, cur.sub, src);
-    if (lane == 0) {
-      if (blk < 0 || blk >= a.NB) {
-        flag_error(a.status, PA_ERR_BLOCK_ID);
-        blk = 0;
-      }
-      const int row = blk * a.KVH + kvh;
-      uint64_t* bar = &wbar[s];
-      uint8_t* kd = k_tiles + (warp * DEPTH + s) * C::KT;
-      uint8_t* vd = v_tiles + (warp * DEPTH + s) * C::VT;
-      mbar_arrive_expect_tx(bar, C::TX);
-      if constexpr (I8) {
-        tma_load_3d(kd, &tm_k, bar, sub * 128, 0, row);
-      } else {
-        tma_load_4d(kd, &tm_k, bar, 0, sub * 2, 0, row);
-      }
-      if (a.bulk) {
-        bulk_g2s(vd, a.v_base + (size_t)row * C::VT, C::VT, bar);
-        if constexpr (I8) {
-          uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
-          bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
-          bulk_g2s(sd + kVsOff, a.vs_base + (size_t)row * kSubTokens, 64, bar);
-        }
-      } else {
-        tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
-        if constexpr (I8) {
-          uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
-          tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
-          tma_load_2d(sd + kVsOff, &tm_vs, bar, sub * kSubTokens, row);
-        }
-      }
-    }
-  };
-
-  const int npro = n < DEPTH ? n : DEPTH;
-  __syncwarp();
-  for (int j = 0; j < npro; ++j) issue(j, j);
-  int issued = npro;
-
-  // ---- 4. Consumer state ---------------------------------------------------------------------
+  // ---- 3. Consumer position and the first piece's q rows --------------------------------------
   int cb, cseg, csp;
   locate((int)p0, cb, cseg, csp);
   int cpg = pages_of(cb);
   int cctx = s_ctx[cb];
-  int piece_sp0 = csp;
   const float qs = a.qk_scale_log2;
 
   // Q fragments. FP16 cache: fp16 A fragments of the m16n8k16 MMA (qa rows g, qb rows g+8).
@@ -583,9 +517,28 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // most qsc / 508 per element), held as A fragments of the integer m16n8k32 MMA, so raw K
   // bytes feed the tensor cores with no unpacking: x = {q1 lo, q1 hi, q2 lo, q2 hi}.
   uint4 qa[NS], qb[NS];
+  uint4 ra[NS], rb[NS];  // raw fp16 q rows, fetched ahead of their conversion
   float qsc0 = 0.f, qsc1 = 0.f;
   int q_b = -1, q_seg = -1;
 
+  auto fetch_q = [&](int b, int seg) {
+    const int kvh = seg / a.HT;
+    const int ht = seg - kvh * a.HT;
+    const int hl = ht * GT + g;
+    const __half* qrow = a.q + ((size_t)b * a.H + (size_t)kvh * a.G + hl) * D;
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const int c = I8 ? chunk_i8(r, si) : chunk_f16(r, si);
+      ra[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
+                          : make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (GT == 16) {
+        rb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
+                                : make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        rb[si] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  };
   auto split_row = [&](const uint4 (&src)[NS], uint4 (&dst)[NS], float& qsc) {
     float amax = 0.f;
 #pragma unroll
@@ -623,24 +576,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
-  auto load_q = [&](int b, int seg) {
-    const int kvh = seg / a.HT;
-    const int ht = seg - kvh * a.HT;
-    const int hl = ht * GT + g;
-    const __half* qrow = a.q + ((size_t)b * a.H + (size_t)kvh * a.G + hl) * D;
-    uint4 ra[NS], rb[NS];
-#pragma unroll
-    for (int si = 0; si < NS; ++si) {
-      const int c = I8 ? chunk_i8(r, si) : chunk_f16(r, si);
-      ra[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
-                          : make_uint4(0u, 0u, 0u, 0u);
-      if constexpr (GT == 16) {
-        rb[si] = (hl + 8 < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * D + 8 * c))
-                                : make_uint4(0u, 0u, 0u, 0u);
-      } else {
-        rb[si] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
+  auto convert_q = [&]() {
     if constexpr (I8) {
       split_row(ra, qa, qsc0);
       if constexpr (GT == 16) {
@@ -657,6 +593,76 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   };
+  // The first piece's q rows are requested before the page copies, so their latency overlaps
+  // the block-table reads and the first copies rather than queueing behind them.
+  fetch_q(cb, cseg);
+  q_b = cb;
+  q_seg = cseg;
+
+  // ---- 4. Producer: the copies of 32 upcoming pages, one per lane, as (row << 3) | subpage,
+  // where row = block * kv_heads + kv_head indexes [num_blocks * kv_heads] page rows.
+  auto batch_info = [&](int jbase) {
+    int pk = 0;
+    const int j = jbase + lane;
+    if (j < n) {
+      int b, seg, sp;
+      locate((int)(p0 + j), b, seg, sp);
+      const int kvh = seg / a.HT;
+      const int bi = sp / a.subs;
+      const int sub = sp - bi * a.subs;
+      int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + bi);
+      if (blk < 0 || blk >= a.NB) {
+        flag_error(a.status, PA_ERR_BLOCK_ID);
+        blk = 0;
+      }
+      pk = ((blk * a.KVH + kvh) << 3) | sub;
+    }
+    return pk;
+  };
+  int cur = batch_info(0);
+  int nxt = batch_info(32);
+
+  auto issue = [&](int j, int s) {
+    if (j > 0 && (j & 31) == 0) {
+      cur = nxt;
+      nxt = batch_info(j + 32);
+    }
+    const int pk = __shfl_sync(0xffffffffu, cur, j & 31);
+    if (lane == 0) {
+      const int row = pk >> 3;
+      const int sub = pk & 7;
+      uint64_t* bar = &wbar[s];
+      uint8_t* kd = k_tiles + (warp * DEPTH + s) * C::KT;
+      uint8_t* vd = v_tiles + (warp * DEPTH + s) * C::VT;
+      mbar_arrive_expect_tx(bar, C::TX);
+      if constexpr (I8) {
+        tma_load_3d(kd, &tm_k, bar, sub * 128, 0, row);
+      } else {
+        tma_load_4d(kd, &tm_k, bar, 0, sub * 2, 0, row);
+      }
+      if (a.bulk) {
+        bulk_g2s(vd, a.v_base + (size_t)row * C::VT, C::VT, bar);
+        if constexpr (I8) {
+          uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
+          bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
+          bulk_g2s(sd + kVsOff, a.vs_base + (size_t)row * kSubTokens, 64, bar);
+        }
+      } else {
+        tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
+        if constexpr (I8) {
+          uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
+          tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
+          tma_load_2d(sd + kVsOff, &tm_vs, bar, sub * kSubTokens, row);
+        }
+      }
+    }
+  };
+
+  const int npro = n < DEPTH ? n : DEPTH;
+  __syncwarp();
+  for (int j = 0; j < npro; ++j) issue(j, j);
+  int issued = npro;
+  convert_q();
 
   // Shared-memory offsets of the K cells this lane reads (chunk of load si, token of n-tile
   // jt), fixed for the whole kernel.
@@ -687,37 +693,40 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   int jfail = -1;
   int s = 0;        // ring stage of page j
   uint32_t ph = 0;  // its mbarrier phase parity
-  for (int j = 0; j < n; ++j) {
-    const bool split = (a.mode == kModeSplit);
-    const bool first = (j == 0) || (split ? (csp % kSplitPages == 0) : (csp == 0));
-    const bool last = (j == n - 1) || (csp == cpg - 1) ||
-                      (split && (csp % kSplitPages) == kSplitPages - 1);
-    if (first) {
-      if (q_b != cb || q_seg != cseg) {
-        load_q(cb, cseg);
-        q_b = cb;
-        q_seg = cseg;
-      }
-      m0 = neg_inf();
-      l0 = 0.f;
-      m1 = neg_inf();
-      l1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < MT; ++i)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) oacc[i][nt][e] = 0.f;
-      piece_sp0 = csp;
+  const bool split = (a.mode == kModeSplit);
+  int j = 0;
+  while (j < n) {
+    // ---- one piece: the pages of this warp's range inside one segment (one split in split
+    // mode), subpages [csp, csp + len) of sequence cb, segment cseg.
+    const int piece_sp0 = csp;
+    int len = cpg - csp;
+    if (split) len = min(len, kSplitPages - csp % kSplitPages);
+    len = min(len, n - j);
+    if (q_b != cb || q_seg != cseg) {
+      fetch_q(cb, cseg);
+      convert_q();
+      q_b = cb;
+      q_seg = cseg;
     }
+    m0 = neg_inf();
+    l0 = 0.f;
+    m1 = neg_inf();
+    l1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) oacc[i][nt][e] = 0.f;
 
+    for (int k = 0; k < len; ++k) {
     if (!mbar_wait_bounded(&wbar[s], ph, a.status)) {
       jfail = j;
       break;
     }
 
     // ---- stage -> registers, then hand the stage back to the TMA right away -------------------
-    const int valid = min(kSubTokens, cctx - csp * kSubTokens);
+    const int valid = min(kSubTokens, cctx - (csp + k) * kSubTokens);
     const uint32_t kb = kbase + s * C::KT;
     const uint32_t vb = vbase + s * C::VT;
     const uint32_t sb = sbase + s * C::ST;
@@ -941,7 +950,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
 
-    if (last) {
+    ++j;
+    if (++s == DEPTH) {
+      s = 0;
+      ph ^= 1u;
+    }
+    }  // pages of the piece
+    if (jfail >= 0) break;
+    csp += len;
+
+    {
       // ---- piece epilogue ---------------------------------------------------------------------
       float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
       lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
@@ -979,7 +997,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
       if (split) {
         write_slot(a.part + ((size_t)segid * a.s_max + piece_sp0 / kSplitPages) * SLOT);
-      } else if (piece_sp0 == 0 && csp == cpg - 1) {
+      } else if (piece_sp0 == 0 && csp == cpg) {
         // The whole segment was this warp's: normalise and store directly.
         if (a.mode == kModeStream) {
           const float inv0 = 1.f / lt0;
@@ -1043,28 +1061,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
 
-    // Advance the consumer iterator and the ring stage.
-    if (++csp == cpg) {
+    // ---- next segment
+    if (csp == cpg) {
       csp = 0;
       if (++cseg == SEGS) {
         cseg = 0;
-        if (j + 1 < n) {
+        if (j < n) {
           do { ++cb; } while (pages_of(cb) == 0);
           cctx = s_ctx[cb];
         }
       }
-      if (j + 1 < n) cpg = pages_of(cb);
-    }
-    if (++s == DEPTH) {
-      s = 0;
-      ph ^= 1u;
+      if (j < n) cpg = pages_of(cb);
     }
   }
 
   if (jfail >= 0) {
     // Let copies still in flight land before the CTA's shared memory is released.
-    for (int j = jfail; j < issued; ++j) {
-      (void)mbar_wait_bounded(&wbar[j % DEPTH], (uint32_t)(j / DEPTH) & 1u, nullptr);
+    for (int jj = jfail; jj < issued; ++jj) {
+      (void)mbar_wait_bounded(&wbar[jj % DEPTH], (uint32_t)(jj / DEPTH) & 1u, nullptr);
     }
   }
   }  // n > 0
