@@ -382,6 +382,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   if (threadIdx.x == 0) {
     s_empty = 0;
+    // This CTA's share of the block tables and q rows into L2, so the first block-id and q
+    // reads after the scan do not each wait for DRAM.
+    prefetch_l2_share(a.block_table, (size_t)a.B * a.max_blocks * sizeof(int), blockIdx.x,
+                      gridDim.x);
+    prefetch_l2_share(a.q, (size_t)a.B * a.H * D * sizeof(__half), blockIdx.x, gridDim.x);
     prefetch_tensormap(&tm_k);
     if (!a.bulk) {
       prefetch_tensormap(&tm_v);
@@ -1033,13 +1038,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       } else {
         // A piece of a segment shared with neighbouring warps.
         write_slot(a.part + ((size_t)wg * 2 + (piece_sp0 == 0 ? 1 : 0)) * SLOT);
-        __threadfence();
         __syncwarp();
         int old = 0;
-        if (lane == 0) {
-          __threadfence();
-          old = atomicAdd(a.counters + segid, 1);
-        }
+        // Release this piece; the arrival that completes the count acquires all of them.
+        if (lane == 0) old = atom_add_acq_rel_gpu(a.counters + segid, 1);
         old = __shfl_sync(0xffffffffu, old, 0);
         const long long s_start = (long long)s_pre[cb] + (long long)cseg * cpg;
         const long long s_end = s_start + cpg;
@@ -1084,6 +1086,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }  // n > 0
 
   // ---- 5. Merges of the segments whose last piece this CTA's warps finished ------------------
+  // The pieces of a recorded merge are visible: the recording arrival acquired them, and the
+  // barrier below orders that arrival before every warp's reads.
   // Segments with few pieces are merged one per warp, in parallel; larger ones by the whole
   // CTA together.
   if (lane == 0) s_npend[warp] = npend;
@@ -1104,7 +1108,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       if (np > kWarpMerge) continue;
       if ((idx++ % WARPS) != warp) continue;
       const int segid = pe[0], wf = pe[1], b = pe[3], hbase = pe[4], hcnt = pe[5];
-      __threadfence();
       auto piece = [&](int k) -> const float* {
         return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
       };
@@ -1123,7 +1126,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       const int* pe = s_pend[w][e];
       const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
       if (np <= kWarpMerge) continue;
-      __threadfence();
       if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) >
           (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST)) {
         if (threadIdx.x == 0) flag_error(a.status, PA_ERR_WORKSPACE);

@@ -88,6 +88,36 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Atomic add with acquire-release semantics at GPU scope: the caller's earlier writes (and,
+// through a preceding __syncwarp, its warp's) are visible to whoever observes the new value,
+// and what the caller reads afterwards sees everything released before the values it observed.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// Hint: bring [p, p + bytes) into L2 (p and bytes multiples of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetch this CTA's share of a read-only array into L2 (only whole 16-byte units that lie
+// inside the array).
+__device__ __forceinline__ void prefetch_l2_share(const void* base, size_t bytes, int part,
+                                                  int parts) {
+  const uintptr_t lo = ((uintptr_t)base + 15) & ~(uintptr_t)15;
+  const uintptr_t hi = ((uintptr_t)base + bytes) & ~(uintptr_t)15;
+  if (hi <= lo) return;
+  const size_t units = (hi - lo) >> 4;
+  const size_t per = (units + parts - 1) / parts;
+  const size_t u0 = per * part;
+  if (u0 >= units) return;
+  const size_t n = (units - u0) < per ? (units - u0) : per;
+  prefetch_l2_bulk(reinterpret_cast<const void*>(lo + (u0 << 4)), (uint32_t)(n << 4));
+}
+
 // ------------------------------------------------------------------------------------------
 // TMA: 1-D bulk copies and tiled tensor copies into this CTA's shared memory, completing on an mbarrier
 // ------------------------------------------------------------------------------------------
