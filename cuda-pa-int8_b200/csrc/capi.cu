@@ -382,6 +382,7 @@ const char* pa_status_string(int status) {
   if (status & PA_ERR_BLOCK_ID) return "block_table entry outside [0, num_blocks)";
   if (status & PA_ERR_TIMEOUT) return "device wait timed out";
   if (status & PA_ERR_SLOT) return "slot_mapping entry outside the cache";
+  if (status & PA_ERR_Q_RANGE) return "bf16 q value outside the fp16 range (saturated)";
   return "unknown status";
 }
 
@@ -455,6 +456,75 @@ int pa_splitk_i8(void* out, const void* q, const void* k_cache, const void* v_ca
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
                      workspace_bytes, stream);
+}
+
+// BF16 activations: q (bf16) -> fp16 copy in the workspace, the fp16-q decode into an fp16
+// output in the workspace, then -> bf16 out. Layout: [decode workspace | q fp16 | out fp16],
+// each part 256-byte aligned.
+static size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+size_t pa_decode_bf16q_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads,
+                                       int head_dim, int max_blocks_per_seq, int block_size,
+                                       int kv_dtype, int splitk) {
+  const size_t base = pa_decode_workspace_bytes(num_seqs, num_heads, num_kv_heads, head_dim,
+                                                max_blocks_per_seq, block_size, kv_dtype, splitk);
+  if (base == 0 || num_seqs < 0) return 0;
+  const size_t act = round256((size_t)num_seqs * num_heads * head_dim * 2);
+  return round256(base) + 2 * act;
+}
+
+int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v_cache,
+                    const float* k_scales, const float* v_scales, const int32_t* block_table,
+                    const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                    int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                    int kv_dtype, int splitk, float scale, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (kv_dtype != PA_DTYPE_F16 && kv_dtype != PA_DTYPE_I8)
+    return fail(PA_ERR_UNSUPPORTED, "kv_dtype must be PA_DTYPE_F16 or PA_DTYPE_I8");
+  int rc = check_common(num_seqs, num_heads, num_kv_heads, head_dim, num_blocks, block_size,
+                        max_blocks_per_seq);
+  if (rc != PA_OK) return rc;
+  if (num_seqs == 0) return PA_OK;
+  if (out == nullptr || q == nullptr || workspace == nullptr)
+    return fail(PA_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(out, 16) || !aligned(q, 16) || !aligned(workspace, 256))
+    return fail(PA_ERR_INVALID_ARG, "tensors must be 16-byte aligned (workspace 256-byte)");
+  const size_t need = pa_decode_bf16q_workspace_bytes(num_seqs, num_heads, num_kv_heads,
+                                                      head_dim, max_blocks_per_seq, block_size,
+                                                      kv_dtype, splitk);
+  if (need == 0) return fail(PA_ERR_UNSUPPORTED, "unsupported decode shape");
+  if (workspace_bytes < need)
+    return fail(PA_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+  const size_t base = round256(pa_decode_workspace_bytes(num_seqs, num_heads, num_kv_heads,
+                                                         head_dim, max_blocks_per_seq,
+                                                         block_size, kv_dtype, splitk));
+  const long long n = (long long)num_seqs * num_heads * head_dim;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* q16 = ws + base;
+  void* o16 = ws + base + round256((size_t)n * 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = num_sms_current(nullptr);
+  if (sms <= 0) return fail(PA_ERR_CUDA, "cannot query the current device");
+  cudaError_t e = pa::launch_bf16_to_f16(q, q16, n, reinterpret_cast<int*>(ws), sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "q conversion launch");
+  const int mode = splitk ? pa::kModeSplit : pa::kModeStream;
+  const int kv_i8 = kv_dtype == PA_DTYPE_I8 ? 1 : 0;
+  rc = decode_impl(mode, kv_i8, o16, nullptr, q16, k_cache, v_cache, k_scales, v_scales,
+                   block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
+                   num_blocks, block_size, max_blocks_per_seq, scale, workspace, base, stream);
+  if (rc != PA_OK) return rc;
+  e = pa::launch_f16_to_bf16(o16, out, n, sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "output conversion launch");
+  return PA_OK;
+}
+
+int pa_selftest_bounded_wait(void* workspace, void* stream) {
+  if (workspace == nullptr || !aligned(workspace, 4))
+    return fail(PA_ERR_INVALID_ARG, "workspace must be a non-null, 4-byte aligned pointer");
+  cudaError_t e = pa::launch_selftest_wait(static_cast<int*>(workspace),
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "self-test launch");
+  return PA_OK;
 }
 
 int pa_partial_floats(int num_heads, int num_kv_heads, int head_dim) {

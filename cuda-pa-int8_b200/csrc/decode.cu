@@ -1243,6 +1243,24 @@ cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensor
                  : launch_one<0, 16>(a, maps, grid, stream);
 }
 
+namespace {
+__global__ void selftest_wait_kernel(int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  // Nothing arrives on the barrier: phase 0 never completes, so the bounded wait gives up.
+  (void)mbar_wait_bounded(&bar, 0u, status);
+}
+}  // namespace
+
+cudaError_t launch_selftest_wait(int* status, cudaStream_t st) {
+  selftest_wait_kernel<<<1, 32, 0, st>>>(status);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_reduce(int gt, const ReduceArgs& a, int max_pieces, cudaStream_t stream) {
   const int segs = a.B * a.KVH * a.HT;
   if (segs == 0) return cudaSuccess;

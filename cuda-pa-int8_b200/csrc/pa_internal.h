@@ -76,6 +76,15 @@ cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float*
                                 int semantics, unsigned int* scratch, int num_sms,
                                 cudaStream_t st);
 
+// bf16 <-> fp16 activation conversions (n a multiple of 8, 16-byte aligned buffers).
+cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, int* status, int num_sms,
+                               cudaStream_t st);
+cudaError_t launch_f16_to_bf16(const void* in, void* out, long long n, int num_sms,
+                               cudaStream_t st);
+// One warp waits on an mbarrier that nothing completes; the bounded wait must give up after
+// about a second and set PA_ERR_TIMEOUT in *status (exercises the failure path).
+cudaError_t launch_selftest_wait(int* status, cudaStream_t st);
+
 // Record a message for pa_last_error() and return `code` (defined in capi.cu).
 int fail_status(int code, const char* fmt, ...);
 

@@ -398,4 +398,77 @@ cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float*
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------
+// bf16 <-> fp16 activation conversions around the decode (BF16-q entry point). A bf16 value
+// whose magnitude is inside the fp16 normal range converts exactly (8 significant bits fit
+// in fp16's 11); larger magnitudes saturate to +-65504 and set PA_ERR_Q_RANGE; smaller ones
+// round to fp16 subnormals. The fp16 decode output converts to bf16 with one rounding.
+// ---------------------------------------------------------------------------------------
+__global__ void bf16_to_f16_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
+                                   long long n8, int* status) {
+  bool bad = false;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const uint4 w = in[i];
+    const uint32_t src[4] = {w.x, w.y, w.z, w.w};
+    uint32_t dst[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&src[e]));
+      float a = f.x, b = f.y;
+      if (fabsf(a) > 65504.f) {
+        bad = true;
+        a = copysignf(65504.f, a);
+      }
+      if (fabsf(b) > 65504.f) {
+        bad = true;
+        b = copysignf(65504.f, b);
+      }
+      const __half2 h = __floats2half2_rn(a, b);
+      dst[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    out[i] = make_uint4(dst[0], dst[1], dst[2], dst[3]);
+  }
+  if (bad) flag_error(status, PA_ERR_Q_RANGE);
+}
+
+__global__ void f16_to_bf16_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
+                                   long long n8) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const uint4 w = in[i];
+    const uint32_t src[4] = {w.x, w.y, w.z, w.w};
+    uint32_t dst[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&src[e]));
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
+      dst[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    out[i] = make_uint4(dst[0], dst[1], dst[2], dst[3]);
+  }
+}
+
+cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, int* status, int num_sms,
+                               cudaStream_t st) {
+  const long long n8 = n / 8;
+  if (n8 == 0) return cudaSuccess;
+  long long want = (n8 + 255) / 256;
+  const int grid = (int)(want < num_sms * 4LL ? want : num_sms * 4LL);
+  bf16_to_f16_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4*>(in),
+                                           static_cast<uint4*>(out), n8, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f16_to_bf16(const void* in, void* out, long long n, int num_sms,
+                               cudaStream_t st) {
+  const long long n8 = n / 8;
+  if (n8 == 0) return cudaSuccess;
+  long long want = (n8 + 255) / 256;
+  const int grid = (int)(want < num_sms * 4LL ? want : num_sms * 4LL);
+  f16_to_bf16_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4*>(in),
+                                           static_cast<uint4*>(out), n8);
+  return cudaGetLastError();
+}
+
 }  // namespace pa

@@ -22,6 +22,7 @@ PA_ERR_CONTEXT_RANGE = 32
 PA_ERR_BLOCK_ID = 64
 PA_ERR_TIMEOUT = 128
 PA_ERR_SLOT = 256
+PA_ERR_Q_RANGE = 512
 
 PA_DTYPE_F16 = 0
 PA_DTYPE_BF16 = 1
@@ -54,6 +55,10 @@ SIGNATURES = {
                                    _vp]),
     "pa_splitk_i8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
                           _vp, _sz, _vp]),
+    "pa_decode_bf16q_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
+    "pa_decode_bf16q": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,
+                             _i, _i, _f, _vp, _sz, _vp]),
+    "pa_selftest_bounded_wait": (_i, [_vp, _vp]),
     "pa_partial_floats": (_i, [_i, _i, _i]),
     "pa_decode_partial": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                                _i, _i, _f, _vp, _sz, _vp]),

@@ -96,9 +96,11 @@ def _require(cond, msg):
 
 
 def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
-                       int8, k_scales, v_scales, validate, out_required=True):
+                       int8, k_scales, v_scales, validate, out_required=True,
+                       act_dtype=torch.float16):
     _require(q.is_cuda and (out is None or out.is_cuda), "tensors must be on CUDA")
-    _require(q.dtype == torch.float16, "q must be fp16")
+    act_name = "fp16" if act_dtype == torch.float16 else "bf16"
+    _require(q.dtype == act_dtype, f"q must be {act_name}")
     if int8:
         _require(k_cache.dtype == torch.int8, "k_cache must be int8")
         _require(v_cache.dtype == torch.int8, "v_cache must be int8")
@@ -121,8 +123,8 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
     _require(q.dim() == 3, "q must be [num_seqs, num_heads, head_dim]")
     B, H, D = q.shape
     if out is not None:
-        _require(tuple(out.shape) == (B, H, D) and out.dtype == torch.float16,
-                 "out must be fp16 with the shape of q")
+        _require(tuple(out.shape) == (B, H, D) and out.dtype == act_dtype,
+                 f"out must be {act_name} with the shape of q")
     _require(k_cache.dim() == 5, "k_cache must be [num_blocks, kv_heads, head_dim/x, block_size, x]")
     NB, KVH, DX, BS, x = k_cache.shape
     if int8:
@@ -187,6 +189,38 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
                     block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D, NB,
                     block_size, max_blocks, float(scale), ws.data_ptr(), ws.numel(), stream)
         _lib.check(rc, "paged decode")
+    return out
+
+
+def decode_bf16(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
+                k_scales=None, v_scales=None, splitk=False, validate=True):
+    """decode() with bf16 activations: q and out are bf16, the cache fp16 or per-token INT8.
+
+    q is converted to fp16 on the device (exact for magnitudes in the fp16 normal range; larger
+    values saturate and set the PA_ERR_Q_RANGE status bit), the fp16 decode runs, and the output
+    is rounded once to bf16.
+    """
+    int8 = k_scales is not None or k_cache.dtype == torch.int8
+    B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
+                                          block_size, int8, k_scales, v_scales, validate,
+                                          act_dtype=torch.bfloat16)
+    if B == 0:
+        return out
+    L = _lib.lib()
+    max_blocks = block_table.shape[1]
+    with _Guard(q.device):
+        kv = _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16
+        need = L.pa_decode_bf16q_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv,
+                                                 1 if splitk else 0)
+        _require(need > 0, "unsupported decode shape: " + _lib.last_error())
+        ws = workspace(q.device, need)
+        rc = L.pa_decode_bf16q(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(),
+                               v_cache.data_ptr(), _ptr(k_scales) if int8 else None,
+                               _ptr(v_scales) if int8 else None, block_table.data_ptr(),
+                               context_lens.data_ptr(), B, H, KVH, D, NB, block_size, max_blocks,
+                               kv, 1 if splitk else 0, float(scale), ws.data_ptr(), ws.numel(),
+                               _stream(q.device))
+        _lib.check(rc, "paged decode (bf16 q)")
     return out
 
 

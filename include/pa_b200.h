@@ -46,6 +46,7 @@ extern "C" {
 #define PA_ERR_BLOCK_ID 64      /* device: a block_table entry outside [0, num_blocks) */
 #define PA_ERR_TIMEOUT 128      /* device: a bounded wait gave up (about one second) */
 #define PA_ERR_SLOT 256         /* device: a slot_mapping entry outside the cache */
+#define PA_ERR_Q_RANGE 512      /* device: a bf16 q value outside the fp16 range (saturated) */
 
 /* ---- dtype codes ---- */
 #define PA_DTYPE_F16 0
@@ -138,6 +139,29 @@ int pa_decode_f16_noalloc(void* out, const void* q, const void* k_cache, const v
  * Generalises the partition kernel of kernels/paged_attention_v4_splitk.cu:28-153 from a
  * token split inside one GPU to a token range owned by one GPU.
  * ---------------------------------------------------------------------------------- */
+/* Decode with bf16 activations: q and out are bf16 [num_seqs, num_heads, head_dim]; the cache
+ * is fp16 (kv_dtype PA_DTYPE_F16) or per-token int8 (PA_DTYPE_I8, with k_scales/v_scales);
+ * splitk selects the split-K pair. q is converted to fp16 on the device (exact for magnitudes
+ * in the fp16 normal range; larger values saturate and set PA_ERR_Q_RANGE in the status word),
+ * the fp16 decode runs, and its output is rounded once to bf16. The workspace holds the decode
+ * workspace followed by the fp16 copies: size it with pa_decode_bf16q_workspace_bytes. This is
+ * the BF16-q support the reference lists as future work (report/benchmark_report.md:196-197);
+ * the reference's own ops take fp16 q only. */
+size_t pa_decode_bf16q_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads,
+                                       int head_dim, int max_blocks_per_seq, int block_size,
+                                       int kv_dtype, int splitk);
+int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v_cache,
+                    const float* k_scales, const float* v_scales, const int32_t* block_table,
+                    const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                    int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                    int kv_dtype, int splitk, float scale, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Failure-path self-test: one warp waits on a barrier that nothing completes; the bounded wait
+ * gives up after about a second and ORs PA_ERR_TIMEOUT into the status word at workspace[0].
+ * The context stays usable. No counterpart in the reference. */
+int pa_selftest_bounded_wait(void* workspace, void* stream);
+
 int pa_partial_floats(int num_heads, int num_kv_heads, int head_dim);
 int pa_decode_partial(int kv_dtype, float* partials, const void* q, const void* k_cache,
                       const void* v_cache, const float* k_scales, const float* v_scales,
