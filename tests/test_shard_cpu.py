@@ -112,3 +112,39 @@ def test_split_context_exchange_gloo_world2():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = sorted(q.get(timeout=5) for _ in range(2))
     assert all(err < 1e-5 for _, err in res), res
+
+
+def _dead_peer_worker(rank, world, port, result_q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        # This rank fails between steps, before the exchange, without joining it.
+        os._exit(3)
+    local = torch.zeros(8)
+    gathered = [torch.empty_like(local) for _ in range(world)]
+    try:
+        dist.all_gather(gathered, local)
+        result_q.put((rank, "completed"))
+    except Exception as e:  # noqa: BLE001 - any backend error is the expected outcome
+        result_q.put((rank, "error: " + type(e).__name__))
+    os._exit(0)
+
+
+def test_split_context_exchange_reports_a_dead_peer():
+    """A rank that dies before the all-gather of partials makes the surviving rank's exchange
+    fail with an error (within the process group's short timeout) instead of hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert procs[1].exitcode == 3
+    assert procs[0].exitcode == 0, procs[0].exitcode
+    rank, outcome = q.get(timeout=5)
+    assert rank == 0 and outcome.startswith("error"), outcome
