@@ -130,6 +130,9 @@ def _dead_peer_worker(rank, world, port, result_q):
         result_q.put((rank, "completed"))
     except Exception as e:  # noqa: BLE001 - any backend error is the expected outcome
         result_q.put((rank, "error: " + type(e).__name__))
+    # Flush the queue's feeder thread before leaving without the process group's teardown.
+    result_q.close()
+    result_q.join_thread()
     os._exit(0)
 
 
