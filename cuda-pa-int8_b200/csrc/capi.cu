@@ -350,6 +350,12 @@ int check_in_dtype(int dt) {
 }
 
 int elem_size(int dt) { return dt == PA_DTYPE_F32 ? 4 : (dt == PA_DTYPE_I8 ? 1 : 2); }
+// Cache kind of the decode kernels: 0 fp16, 1 int8, 2 fp8 e4m3 (-1: not a cache dtype).
+int kv_kind(int kv_dtype) {
+  return kv_dtype == PA_DTYPE_F16 ? 0
+         : kv_dtype == PA_DTYPE_I8 ? 1
+         : kv_dtype == PA_DTYPE_FP8E4M3 ? 2 : -1;
+}
 
 }  // namespace
 
@@ -393,7 +399,8 @@ size_t pa_decode_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, 
                    max_blocks_per_seq) != PA_OK)
     return 0;
   Shape s;
-  const int kv_i8 = kv_dtype == PA_DTYPE_I8 ? 1 : 0;
+  const int kv_i8 = kv_kind(kv_dtype);
+  if (kv_i8 < 0) return 0;
   const int mode = splitk ? pa::kModeSplit : pa::kModeStream;
   if (make_shape(kv_i8, mode, num_seqs, num_heads, num_kv_heads, head_dim, block_size,
                  max_blocks_per_seq, &s) != PA_OK)
@@ -479,8 +486,8 @@ int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v
                     int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                     int kv_dtype, int splitk, float scale, void* workspace,
                     size_t workspace_bytes, void* stream) {
-  if (kv_dtype != PA_DTYPE_F16 && kv_dtype != PA_DTYPE_I8)
-    return fail(PA_ERR_UNSUPPORTED, "kv_dtype must be PA_DTYPE_F16 or PA_DTYPE_I8");
+  if (kv_kind(kv_dtype) < 0)
+    return fail(PA_ERR_UNSUPPORTED, "kv_dtype must be PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3");
   int rc = check_common(num_seqs, num_heads, num_kv_heads, head_dim, num_blocks, block_size,
                         max_blocks_per_seq);
   if (rc != PA_OK) return rc;
@@ -508,8 +515,7 @@ int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v
   cudaError_t e = pa::launch_bf16_to_f16(q, q16, n, reinterpret_cast<int*>(ws), sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "q conversion launch");
   const int mode = splitk ? pa::kModeSplit : pa::kModeStream;
-  const int kv_i8 = kv_dtype == PA_DTYPE_I8 ? 1 : 0;
-  rc = decode_impl(mode, kv_i8, o16, nullptr, q16, k_cache, v_cache, k_scales, v_scales,
+  rc = decode_impl(mode, kv_kind(kv_dtype), o16, nullptr, q16, k_cache, v_cache, k_scales, v_scales,
                    block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                    num_blocks, block_size, max_blocks_per_seq, scale, workspace, base, stream);
   if (rc != PA_OK) return rc;
@@ -527,6 +533,28 @@ int pa_selftest_bounded_wait(void* workspace, void* stream) {
   return PA_OK;
 }
 
+int pa_decode_fp8(void* out, const void* q, const void* k_cache, const void* v_cache,
+                  const float* k_scales, const float* v_scales, const int32_t* block_table,
+                  const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                  float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_impl(pa::kModeStream, 2, out, nullptr, q, k_cache, v_cache, k_scales, v_scales,
+                     block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
+                     num_blocks, block_size, max_blocks_per_seq, scale, workspace,
+                     workspace_bytes, stream);
+}
+
+int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_cache,
+                  const float* k_scales, const float* v_scales, const int32_t* block_table,
+                  const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                  float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_impl(pa::kModeSplit, 2, out, nullptr, q, k_cache, v_cache, k_scales, v_scales,
+                     block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
+                     num_blocks, block_size, max_blocks_per_seq, scale, workspace,
+                     workspace_bytes, stream);
+}
+
 int pa_partial_floats(int num_heads, int num_kv_heads, int head_dim) {
   if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return 0;
   const int G = num_heads / num_kv_heads;
@@ -540,9 +568,9 @@ int pa_decode_partial(int kv_dtype, float* partials, const void* q, const void* 
                       int num_heads, int num_kv_heads, int head_dim, int num_blocks,
                       int block_size, int max_blocks_per_seq, float scale, void* workspace,
                       size_t workspace_bytes, void* stream) {
-  if (kv_dtype != PA_DTYPE_F16 && kv_dtype != PA_DTYPE_I8)
-    return fail(PA_ERR_UNSUPPORTED, "kv dtype must be fp16 or int8");
-  return decode_impl(pa::kModePartial, kv_dtype == PA_DTYPE_I8 ? 1 : 0, nullptr, partials, q,
+  if (kv_kind(kv_dtype) < 0)
+    return fail(PA_ERR_UNSUPPORTED, "kv dtype must be fp16, int8 or fp8 e4m3");
+  return decode_impl(pa::kModePartial, kv_kind(kv_dtype), nullptr, partials, q,
                      k_cache, v_cache, k_scales, v_scales, block_table, context_lens, num_seqs,
                      num_heads, num_kv_heads, head_dim, num_blocks, block_size,
                      max_blocks_per_seq, scale, workspace, workspace_bytes, stream);
@@ -607,6 +635,34 @@ int pa_quantize_into_cache(const void* k, const void* v, int in_dtype, int64_t t
                                         k_fixed_scale, v_fixed_scale, status,
                                         static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return PA_OK;
+}
+
+int pa_quantize_into_cache_fp8(const void* k, const void* v, int in_dtype, int64_t token_stride,
+                               const int32_t* slot_mapping, int num_tokens, int num_kv_heads,
+                               int head_dim, void* k_cache, void* v_cache, float* k_scales,
+                               float* v_scales, int num_blocks, int block_size, int* status,
+                               void* stream) {
+  int rc = check_in_dtype(in_dtype);
+  if (rc != PA_OK) return rc;
+  if (num_tokens == 0) return PA_OK;
+  if (num_tokens < 0 || num_kv_heads <= 0 || num_blocks <= 0 || block_size <= 0)
+    return fail(PA_ERR_INVALID_ARG, "invalid sizes");
+  if (head_dim != 128) return fail(PA_ERR_UNSUPPORTED, "head_dim %d unsupported", head_dim);
+  if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_cache == nullptr ||
+      v_cache == nullptr || k_scales == nullptr || v_scales == nullptr)
+    return fail(PA_ERR_INVALID_ARG, "null pointer argument");
+  if (token_stride < (int64_t)num_kv_heads * head_dim)
+    return fail(PA_ERR_INVALID_ARG, "token_stride smaller than num_kv_heads*head_dim");
+  const size_t es = (size_t)elem_size(in_dtype);
+  if (!aligned(k, es * 4) || !aligned(v, es * 4) || ((size_t)token_stride * es) % (es * 4) != 0 ||
+      !aligned(k_cache, 4) || !aligned(v_cache, 4))
+    return fail(PA_ERR_INVALID_ARG, "misaligned input or cache pointer");
+  cudaError_t e = pa::launch_write_rows(in_dtype, 2, head_dim, k, v, token_stride, slot_mapping,
+                                        num_tokens, num_kv_heads, k_cache, v_cache, k_scales,
+                                        v_scales, num_blocks, block_size, nullptr, nullptr,
+                                        status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 quantize launch");
   return PA_OK;
 }
 

@@ -50,14 +50,16 @@ constexpr int kVsOff = 128;
 
 template <int KVK, int D, int GT, int DEPTH, int WARPS>
 struct Tile {
-  static constexpr bool I8 = KVK == 1;
-  static constexpr int ELEM = I8 ? 1 : 2;
+  static constexpr bool I8 = KVK == 1;    // int8 values, per-token scales
+  static constexpr bool F8 = KVK == 2;    // fp8 e4m3 values, per-token scales
+  static constexpr bool BYTE = KVK != 0;  // one-byte elements (the INT8 page layout)
+  static constexpr int ELEM = BYTE ? 1 : 2;
   static constexpr int KT = D * kSubTokens * ELEM;  // K tile bytes
   static constexpr int VT = D * kSubTokens * ELEM;  // V tile bytes
   // Scale tiles: 16 K scales at +0 and 16 V scales at +128 (tensor-copy destinations are
   // kept 128-byte aligned); 128 bytes of them are transferred per stage.
-  static constexpr int ST = I8 ? 256 : 0;
-  static constexpr uint32_t TX = KT + VT + (I8 ? 128 : 0);  // bytes delivered per stage
+  static constexpr int ST = BYTE ? 256 : 0;
+  static constexpr uint32_t TX = KT + VT + (BYTE ? 128 : 0);  // bytes delivered per stage
   static constexpr int NS = D / 32;                 // 8-value K loads per token per lane
   static constexpr int MT = D / 16;                 // PV m-tiles (head_dim rows)
   static constexpr int NT = GT / 8;                 // PV n-tiles (heads)
@@ -349,6 +351,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                   const __grid_constant__ CUtensorMap tm_vs) {
   using C = Tile<KVK, D, GT, DEPTH, WARPS>;
   constexpr bool I8 = C::I8;
+  constexpr bool F8 = C::F8;
+  constexpr bool BYTE = C::BYTE;
   constexpr int NS = C::NS;
   constexpr int MT = C::MT;
   constexpr int NT = C::NT;
@@ -390,7 +394,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     prefetch_tensormap(&tm_k);
     if (!a.bulk) {
       prefetch_tensormap(&tm_v);
-      if constexpr (I8) {
+      if constexpr (BYTE) {
         prefetch_tensormap(&tm_ks);
         prefetch_tensormap(&tm_vs);
       }
@@ -533,7 +537,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const __half* qrow = a.q + ((size_t)b * a.H + (size_t)kvh * a.G + hl) * D;
 #pragma unroll
     for (int si = 0; si < NS; ++si) {
-      const int c = I8 ? chunk_i8(r, si) : chunk_f16(r, si);
+      const int c = BYTE ? chunk_i8(r, si) : chunk_f16(r, si);
       ra[si] = (hl < a.G) ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * c))
                           : make_uint4(0u, 0u, 0u, 0u);
       if constexpr (GT == 16) {
@@ -640,21 +644,21 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       uint8_t* kd = k_tiles + (warp * DEPTH + s) * C::KT;
       uint8_t* vd = v_tiles + (warp * DEPTH + s) * C::VT;
       mbar_arrive_expect_tx(bar, C::TX);
-      if constexpr (I8) {
+      if constexpr (BYTE) {
         tma_load_3d(kd, &tm_k, bar, sub * 128, 0, row);
       } else {
         tma_load_4d(kd, &tm_k, bar, 0, sub * 2, 0, row);
       }
       if (a.bulk) {
         bulk_g2s(vd, a.v_base + (size_t)row * C::VT, C::VT, bar);
-        if constexpr (I8) {
+        if constexpr (BYTE) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
           bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
           bulk_g2s(sd + kVsOff, a.vs_base + (size_t)row * kSubTokens, 64, bar);
         }
       } else {
         tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
-        if constexpr (I8) {
+        if constexpr (BYTE) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
           tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
           tma_load_2d(sd + kVsOff, &tm_vs, bar, sub * kSubTokens, row);
@@ -677,7 +681,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll
     for (int jt = 0; jt < 2; ++jt) {
       const int tau = 4 * (g >> 1) + (g & 1) + 2 * jt;
-      if constexpr (I8) {
+      if constexpr (BYTE) {
         const int c = chunk_i8(r, si);
         koff[si][jt] = c * 128 + ((((tau >> 1) ^ (c & 7)) << 4) | ((tau & 1) << 3));
       } else {
@@ -687,10 +691,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   }
-  const uint32_t voff = I8 ? (uint32_t)(g * 16 + 4 * r) : (uint32_t)((g * 16 + 4 * r) * 2);
+  const uint32_t voff = BYTE ? (uint32_t)(g * 16 + 4 * r) : (uint32_t)((g * 16 + 4 * r) * 2);
   const uint32_t kbase = smem_u32(k_tiles) + warp * DEPTH * C::KT;
   const uint32_t vbase = smem_u32(v_tiles) + warp * DEPTH * C::VT;
-  const uint32_t sbase = I8 ? smem_u32(s_tiles) + warp * DEPTH * C::ST : 0u;
+  const uint32_t sbase = BYTE ? smem_u32(s_tiles) + warp * DEPTH * C::ST : 0u;
 
   float m0 = neg_inf(), l0 = 0.f, m1 = neg_inf(), l1 = 0.f;
   float oacc[MT][NT][4];
@@ -744,13 +748,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     for (int si = 0; si < NS; ++si) {
 #pragma unroll
       for (int jt = 0; jt < 2; ++jt) {
-        if constexpr (I8) k8[si][jt] = lds64(kb + koff[si][jt]);
+        if constexpr (BYTE) k8[si][jt] = lds64(kb + koff[si][jt]);
         else k16[si][jt] = lds128(kb + koff[si][jt]);
       }
     }
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
-      if constexpr (I8) {
+      if constexpr (BYTE) {
         v8[i][0] = lds32(vb + voff + i * 256);
         v8[i][1] = lds32(vb + voff + i * 256 + 128);
       } else {
@@ -758,7 +762,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         v16[i][1] = lds64(vb + voff + i * 512 + 256);
       }
     }
-    if constexpr (I8) {
+    if constexpr (BYTE) {
       ksv = lds128f(sb + 16 * r);
       vsv = lds128f(sb + kVsOff + 16 * r);
     }
@@ -807,6 +811,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           y[0] = y[1] = y[2] = y[3] = 0.f;
         }
       } else {
+        if constexpr (F8) {
+          // e4m3 K bytes -> exact fp16 (every e4m3 value is an fp16 value).
+#pragma unroll
+          for (int si = 0; si < NS; ++si)
+#pragma unroll
+            for (int jt = 0; jt < 2; ++jt) {
+              e4m3x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
+              e4m3x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
+            }
+        }
         // Two accumulation chains per n-tile (even / odd si) shorten the MMA dependency.
         float sacc[2][2][4];
 #pragma unroll
@@ -837,7 +851,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
       // Logits in log2 units.
       float ksc[4] = {qs, qs, qs, qs};
-      if constexpr (I8) {
+      if constexpr (BYTE) {
         ksc[0] = ksv.x * qs;
         ksc[1] = ksv.y * qs;
         ksc[2] = ksv.z * qs;
@@ -909,7 +923,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           py[e] = 0.f;
         }
       }
-      if constexpr (I8) {
+      if constexpr (BYTE) {
         const float vsc[4] = {vsv.x, vsv.y, vsv.z, vsv.w};
         if (valid < kSubTokens) {
           // Scales of slots past the context may hold anything: keep them out of P'.
@@ -944,6 +958,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         if constexpr (I8) {
           i8x4_to_f16x2x2(v8[i][0], a0, a2);
           i8x4_to_f16x2x2(v8[i][1], a1, a3);
+        } else if constexpr (F8) {
+          // e4m3 bytes past the context may be NaN encodings: masked like fp16 V.
+          e4m3x4_to_f16x2x2(v8[i][0], a0, a2);
+          e4m3x4_to_f16x2x2(v8[i][1], a1, a3);
+          a0 &= mlo;
+          a2 &= mhi;
+          a1 &= mlo;
+          a3 &= mhi;
         } else {
           a0 = v16[i][0].x & mlo;
           a2 = v16[i][0].y & mhi;
@@ -1203,6 +1225,8 @@ template <> struct Shape<1, 8> { static constexpr int W = PA_I8_WARPS, DP = PA_I
 template <> struct Shape<0, 8> { static constexpr int W = PA_F16_WARPS, DP = PA_F16_DEPTH; };
 template <> struct Shape<1, 16> { static constexpr int W = 8, DP = 4; };
 template <> struct Shape<0, 16> { static constexpr int W = 8, DP = 3; };
+template <> struct Shape<2, 8> { static constexpr int W = 8, DP = 4; };
+template <> struct Shape<2, 16> { static constexpr int W = 8, DP = 4; };
 
 template <int KVK, int GT>
 cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
@@ -1229,12 +1253,17 @@ cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
 }  // namespace
 
 int decode_warps_per_cta(int kv_i8, int gt) {
+  if (kv_i8 == 2) return gt == 8 ? Shape<2, 8>::W : Shape<2, 16>::W;
   if (kv_i8) return gt == 8 ? Shape<1, 8>::W : Shape<1, 16>::W;
   return gt == 8 ? Shape<0, 8>::W : Shape<0, 16>::W;
 }
 
 cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensorMap* maps,
                           int grid, cudaStream_t stream) {
+  if (kv_i8 == 2) {
+    return gt == 8 ? launch_one<2, 8>(a, maps, grid, stream)
+                   : launch_one<2, 16>(a, maps, grid, stream);
+  }
   if (kv_i8) {
     return gt == 8 ? launch_one<1, 8>(a, maps, grid, stream)
                    : launch_one<1, 16>(a, maps, grid, stream);

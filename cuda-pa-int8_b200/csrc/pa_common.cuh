@@ -13,6 +13,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 
 #include "pa_status.h"
@@ -242,6 +243,15 @@ __device__ __forceinline__ void i8x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32
   const uint32_t u = w ^ 0x80808080u;
   lo = hsub2_bias(prmt(u, 0x64646464u, 0x4140u));
   hi = hsub2_bias(prmt(u, 0x64646464u, 0x4342u));
+}
+
+// Four e4m3 (fp8) bytes -> bytes (0,1) and (2,3) as fp16x2 (low byte -> low half); exact,
+// every e4m3 value being an fp16 value.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const __half2_raw a = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xffffu), __NV_E4M3);
+  const __half2_raw b = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
+  lo = (uint32_t)a.x | ((uint32_t)a.y << 16);
+  hi = (uint32_t)b.x | ((uint32_t)b.y << 16);
 }
 
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {

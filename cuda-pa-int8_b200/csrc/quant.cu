@@ -288,8 +288,67 @@ __global__ void scale_finalize_kernel(const unsigned int* amax_bits, float* scal
   *scale_out = s;
 }
 
+// Token-granular FP8 (e4m3) write, one warp per (token, kv-head, K|V) row: scale =
+// amax / 448 (IEEE fp32 divide), q = e4m3(x / scale) with round-to-nearest-even and saturation
+// to +-448; a zero row stores scale 0 and zeros. Same page layout as the INT8 cache.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) write_rows_fp8_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
+    const int* __restrict__ slot_mapping, int N, int KVH, uint8_t* __restrict__ k_cache,
+    uint8_t* __restrict__ v_cache, float* __restrict__ k_scales, float* __restrict__ v_scales,
+    int NB, int bs, int* status) {
+  constexpr int DPL = D / 32;
+  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long long)N * KVH * 2) return;
+  const int which = (int)(gw & 1);  // 0: K, 1: V
+  const long long row = gw >> 1;
+  const int n = (int)(row / KVH);
+  const int kvh = (int)(row - (long long)n * KVH);
+  const int slot = __ldg(slot_mapping + n);
+  if (slot < 0) return;  // padding token
+  const int blk = slot / bs;
+  const int off = slot - blk * bs;
+  if (blk >= NB) {
+    if (lane == 0) flag_error(status, PA_ERR_SLOT);
+    return;
+  }
+  const T* src = (which ? v : k) + (size_t)n * token_stride + (size_t)kvh * D + lane * DPL;
+  float x[DPL];
+  load_vals<T, DPL>(src, x);
+  float am = 0.f;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) am = fmaxf(am, fabsf(x[e]));
+  am = warp_max(am);
+  const float s = __fdiv_rn(am, 448.f);
+  uint8_t qv[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; ++e)
+    qv[e] = s > 0.f ? (uint8_t)__nv_cvt_float_to_fp8(__fdiv_rn(x[e], s), __NV_SATFINITE,
+                                                     __NV_E4M3)
+                    : (uint8_t)0;
+  const size_t page = (size_t)blk * KVH + kvh;
+  const int d0 = lane * DPL;
+  if (which == 0) {
+    // K [.., D/8, bs, 8]: DPL (<= 8) consecutive d inside one 8-wide chunk.
+    uint8_t* dst = k_cache + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
+    if constexpr (DPL == 4) {
+      *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(qv);
+    } else {
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) dst[e] = qv[e];
+    }
+    if (lane == 0) k_scales[page * bs + off] = s;
+  } else {
+    // V [.., D, bs]: one byte per head_dim row.
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) v_cache[(page * D + d0 + e) * bs + off] = qv[e];
+    if (lane == 0) v_scales[page * bs + off] = s;
+  }
+}
+
 template <typename T>
-cudaError_t launch_rows_t(bool i8, int D, const void* k, const void* v, long long ts,
+cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long long ts,
                           const int* slots, int N, int KVH, void* kc, void* vc, float* ks,
                           float* vs, int NB, int bs, const float* kf, const float* vf,
                           int* status, cudaStream_t st) {
@@ -299,7 +358,11 @@ cudaError_t launch_rows_t(bool i8, int D, const void* k, const void* v, long lon
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
   if (D != 128) return cudaErrorInvalidValue;
-  if (i8) {
+  if (kind == 2) {
+    write_rows_fp8_kernel<T, 128><<<grid, 256, 0, st>>>(
+        kk, vv, ts, slots, N, KVH, static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), ks, vs,
+        NB, bs, status);
+  } else if (kind == 1) {
     write_rows_kernel<T, true, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc, ks,
                                                           vs, NB, bs, kf, vf, status);
   } else {
@@ -333,19 +396,19 @@ cudaError_t launch_prefill_t(bool i8, const void* k, const void* v, int S, int L
 
 }  // namespace
 
-cudaError_t launch_write_rows(int in_dtype, bool i8, int D, const void* k, const void* v,
+cudaError_t launch_write_rows(int in_dtype, int kind, int D, const void* k, const void* v,
                               long long ts, const int* slots, int N, int KVH, void* kc,
                               void* vc, float* ks, float* vs, int NB, int bs, const float* kf,
                               const float* vf, int* status, cudaStream_t st) {
   switch (in_dtype) {
     case PA_DTYPE_F16:
-      return launch_rows_t<__half>(i8, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
+      return launch_rows_t<__half>(kind, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
                                    vf, status, st);
     case PA_DTYPE_BF16:
-      return launch_rows_t<__nv_bfloat16>(i8, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB,
+      return launch_rows_t<__nv_bfloat16>(kind, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB,
                                           bs, kf, vf, status, st);
     case PA_DTYPE_F32:
-      return launch_rows_t<float>(i8, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
+      return launch_rows_t<float>(kind, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
                                   vf, status, st);
     default:
       return cudaErrorInvalidValue;

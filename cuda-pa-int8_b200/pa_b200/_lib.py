@@ -28,6 +28,7 @@ PA_DTYPE_F16 = 0
 PA_DTYPE_BF16 = 1
 PA_DTYPE_F32 = 2
 PA_DTYPE_I8 = 3
+PA_DTYPE_FP8E4M3 = 4
 
 PA_SCALE_CLAMP_THEN_DIVIDE = 0
 PA_SCALE_DIVIDE_THEN_CLAMP = 1
@@ -59,6 +60,12 @@ SIGNATURES = {
     "pa_decode_bf16q": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,
                              _i, _i, _f, _vp, _sz, _vp]),
     "pa_selftest_bounded_wait": (_i, [_vp, _vp]),
+    "pa_decode_fp8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
+                           _vp, _sz, _vp]),
+    "pa_splitk_fp8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
+                           _vp, _sz, _vp]),
+    "pa_quantize_into_cache_fp8": (_i, [_vp, _vp, _i, _i64, _vp, _i, _i, _i, _vp, _vp, _vp, _vp,
+                                        _i, _i, _vp, _vp]),
     "pa_partial_floats": (_i, [_i, _i, _i]),
     "pa_decode_partial": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                                _i, _i, _f, _vp, _sz, _vp]),

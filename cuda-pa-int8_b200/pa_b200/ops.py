@@ -95,15 +95,33 @@ def _require(cond, msg):
         raise RuntimeError(msg)
 
 
+_FP8 = getattr(torch, "float8_e4m3fn", None)
+
+
+def _kv_kind(k_cache, k_scales):
+    """'f8' for an fp8 e4m3 cache, 'i8' for int8 (or whenever scales are given), else 'f16'."""
+    if _FP8 is not None and k_cache.dtype == _FP8:
+        return "f8"
+    return "i8" if (k_scales is not None or k_cache.dtype == torch.int8) else "f16"
+
+
+_KV_CODE = {"f16": _lib.PA_DTYPE_F16, "i8": _lib.PA_DTYPE_I8, "f8": _lib.PA_DTYPE_FP8E4M3}
+
+
 def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
-                       int8, k_scales, v_scales, validate, out_required=True,
+                       kind, k_scales, v_scales, validate, out_required=True,
                        act_dtype=torch.float16):
+    int8 = kind != "f16"  # one-byte cache with per-token scales (int8 or fp8)
     _require(q.is_cuda and (out is None or out.is_cuda), "tensors must be on CUDA")
     act_name = "fp16" if act_dtype == torch.float16 else "bf16"
     _require(q.dtype == act_dtype, f"q must be {act_name}")
-    if int8:
+    if kind == "f8":
+        _require(k_cache.dtype == _FP8, "k_cache must be float8_e4m3fn")
+        _require(v_cache.dtype == _FP8, "v_cache must be float8_e4m3fn")
+    if kind == "i8":
         _require(k_cache.dtype == torch.int8, "k_cache must be int8")
         _require(v_cache.dtype == torch.int8, "v_cache must be int8")
+    if int8:
         _require(k_scales is not None and k_scales.dtype == torch.float32,
                  "k_scales must be fp32")
         _require(v_scales is not None and v_scales.dtype == torch.float32,
@@ -163,22 +181,25 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
     single-pass kernel with the fused combine runs. validate=False skips the one host sync
     that checks context_lens (the kernels still flag bad lengths in the status word).
     """
-    int8 = k_scales is not None or k_cache.dtype == torch.int8
+    kind = _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
-                                          block_size, int8, k_scales, v_scales, validate)
+                                          block_size, kind, k_scales, v_scales, validate)
     if B == 0:
         return out
     L = _lib.lib()
     max_blocks = block_table.shape[1]
     with _Guard(q.device):
-        kv = _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16
+        kv = _KV_CODE[kind]
         need = L.pa_decode_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv,
                                            1 if splitk else 0)
         _require(need > 0, "unsupported decode shape: " + _lib.last_error())
         ws = workspace(q.device, need)
         stream = _stream(q.device)
-        if int8:
-            fn = L.pa_splitk_i8 if splitk else L.pa_decode_i8
+        if kind != "f16":
+            if kind == "f8":
+                fn = L.pa_splitk_fp8 if splitk else L.pa_decode_fp8
+            else:
+                fn = L.pa_splitk_i8 if splitk else L.pa_decode_i8
             rc = fn(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                     k_scales.data_ptr(), v_scales.data_ptr(), block_table.data_ptr(),
                     context_lens.data_ptr(), B, H, KVH, D, NB, block_size, max_blocks,
@@ -200,16 +221,17 @@ def decode_bf16(out, q, k_cache, v_cache, block_table, context_lens, scale, bloc
     values saturate and set the PA_ERR_Q_RANGE status bit), the fp16 decode runs, and the output
     is rounded once to bf16.
     """
-    int8 = k_scales is not None or k_cache.dtype == torch.int8
+    kind = _kv_kind(k_cache, k_scales)
+    int8 = kind != "f16"
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
-                                          block_size, int8, k_scales, v_scales, validate,
+                                          block_size, kind, k_scales, v_scales, validate,
                                           act_dtype=torch.bfloat16)
     if B == 0:
         return out
     L = _lib.lib()
     max_blocks = block_table.shape[1]
     with _Guard(q.device):
-        kv = _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16
+        kv = _KV_CODE[kind]
         need = L.pa_decode_bf16q_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv,
                                                  1 if splitk else 0)
         _require(need > 0, "unsupported decode shape: " + _lib.last_error())
@@ -233,9 +255,9 @@ def decode_partial(q, k_cache, v_cache, block_table, context_lens, scale, block_
     """Un-normalised per-(sequence, kv-head) partials (O, m, l) for this device's token
     ranges: fp32 [num_seqs, num_kv_heads * slot]. Sequences with context 0 give empty
     partials. Used to split one sequence's context across GPUs."""
-    int8 = k_scales is not None or k_cache.dtype == torch.int8
+    kind = _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(None, q, k_cache, v_cache, block_table, context_lens,
-                                          block_size, int8, k_scales, v_scales, validate=False)
+                                          block_size, kind, k_scales, v_scales, validate=False)
     per = partial_floats(H, KVH, D) * KVH  # floats per sequence: kv_heads x head tiles x slot
     if partials is None:
         partials = torch.empty(B, per, dtype=torch.float32, device=q.device)
@@ -246,7 +268,7 @@ def decode_partial(q, k_cache, v_cache, block_table, context_lens, scale, block_
     L = _lib.lib()
     max_blocks = block_table.shape[1]
     with _Guard(q.device):
-        kv = _lib.PA_DTYPE_I8 if int8 else _lib.PA_DTYPE_F16
+        kv = _KV_CODE[kind]
         need = L.pa_decode_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv, 0)
         _require(need > 0, "unsupported decode shape: " + _lib.last_error())
         ws = workspace(q.device, need)
@@ -305,7 +327,14 @@ def quantize_into_cache(key, value, k_cache, v_cache, k_scales, v_scales, slot_m
     per-tensor mode (benchmarks/int8_bridge/paged_cache.py:142-145).
     """
     _check_rows(key, value)
-    _require(k_cache.dtype == torch.int8 and v_cache.dtype == torch.int8, "cache must be int8")
+    fp8 = _FP8 is not None and k_cache.dtype == _FP8
+    if fp8:
+        _require(v_cache.dtype == _FP8, "v_cache must be float8_e4m3fn like k_cache")
+        _require(k_scale is None and v_scale is None,
+                 "the fp8 cache write has per-token scales only")
+    else:
+        _require(k_cache.dtype == torch.int8 and v_cache.dtype == torch.int8,
+                 "cache must be int8")
     _require(k_scales.dtype == torch.float32 and v_scales.dtype == torch.float32,
              "scales must be fp32")
     _require(slot_mapping.dtype == torch.int32 and slot_mapping.is_cuda,
@@ -323,6 +352,14 @@ def quantize_into_cache(key, value, k_cache, v_cache, k_scales, v_scales, slot_m
                      "fixed scales must be one fp32 element on the key's device")
     with _Guard(key.device):
         ws = workspace(key.device, 256)
+        if fp8:
+            rc = _lib.lib().pa_quantize_into_cache_fp8(
+                key.data_ptr(), value.data_ptr(), _DTYPE_CODE[key.dtype], key.stride(0),
+                slot_mapping.data_ptr(), N, KVH, D, k_cache.data_ptr(), v_cache.data_ptr(),
+                k_scales.data_ptr(), v_scales.data_ptr(), k_cache.shape[0], block_size,
+                ws.data_ptr(), _stream(key.device))
+            _lib.check(rc, "quantize_into_cache (fp8)")
+            return
         rc = _lib.lib().pa_quantize_into_cache(
             key.data_ptr(), value.data_ptr(), _DTYPE_CODE[key.dtype], key.stride(0),
             slot_mapping.data_ptr(), N, KVH, D, k_cache.data_ptr(), v_cache.data_ptr(),

@@ -53,6 +53,7 @@ extern "C" {
 #define PA_DTYPE_BF16 1
 #define PA_DTYPE_F32 2
 #define PA_DTYPE_I8 3
+#define PA_DTYPE_FP8E4M3 4 /* fp8 e4m3 cache values with per-token fp32 scales */
 
 /* ---- per-tensor scale semantics for pa_absmax_scale ---- */
 /* quantize_per_tensor (tests/paged_decode_attn.py:115-121): clamp_min(1e-8) in the input
@@ -125,6 +126,21 @@ int pa_splitk_i8(void* out, const void* q, const void* k_cache, const void* v_ca
  * PA_ERR_WORKSPACE. The first call on a device looks up the array's address and should come
  * before any stream capture. Calls share the array: calls that overlap on the GPU race, so
  * order them on one stream. This entry point has no counterpart in the reference. */
+/* FP8 (e4m3) KV cache: the INT8 page layout with e4m3 bytes and per-token fp32 scales
+ * (value = e4m3 * scale; see pa_quantize_into_cache_fp8). Same arguments as pa_decode_i8 /
+ * pa_splitk_i8. The reference lists an FP8 KV variant as future work
+ * (report/benchmark_report.md:196-197) and has no kernel for it. */
+int pa_decode_fp8(void* out, const void* q, const void* k_cache, const void* v_cache,
+                  const float* k_scales, const float* v_scales, const int32_t* block_table,
+                  const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                  float scale, void* workspace, size_t workspace_bytes, void* stream);
+int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_cache,
+                  const float* k_scales, const float* v_scales, const int32_t* block_table,
+                  const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                  float scale, void* workspace, size_t workspace_bytes, void* stream);
+
 int pa_decode_f16_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
                           const int32_t* block_table, const int32_t* context_lens, int num_seqs,
                           int num_heads, int num_kv_heads, int head_dim, int num_blocks,
@@ -194,6 +210,16 @@ int pa_quantize_into_cache(const void* k, const void* v, int in_dtype, int64_t t
                            float* v_scales, int num_blocks, int block_size,
                            const float* k_fixed_scale, const float* v_fixed_scale, int* status,
                            void* stream);
+
+/* Per-token FP8 (e4m3) write, same rows and slots as pa_quantize_into_cache:
+ *   scale = amax / 448 (fp32 IEEE divide; 448 is the largest finite e4m3)
+ *   q     = e4m3(x / scale), round-to-nearest-even, saturating to +-448; a zero row gives
+ *           scale 0 and zeros. */
+int pa_quantize_into_cache_fp8(const void* k, const void* v, int in_dtype, int64_t token_stride,
+                               const int32_t* slot_mapping, int num_tokens, int num_kv_heads,
+                               int head_dim, void* k_cache, void* v_cache, float* k_scales,
+                               float* v_scales, int num_blocks, int block_size, int* status,
+                               void* stream);
 
 /* FP16 copy-into-cache (no quantisation), same slot semantics: the fp16 cache write of
  * PagedKVCache.decode_append / build_paged_kv_cache (paged_cache.py:147-150,

@@ -17,6 +17,11 @@ Each function cites the reference lines it restates:
   split_partials/lse_merge  split-K partition + reduce (kernels/paged_attention_v4_splitk.cu:
                          28-153, 156-187)
   BridgeCacheOracle      benchmarks/int8_bridge/paged_cache.py:41-156
+  quantize_per_token_fp8 / dequantize_fp8: the FP8 (e4m3) cache format of this library,
+                         which has no reference counterpart (the reference lists FP8 KV as
+                         future work, report/benchmark_report.md:196-197); its e4m3 rounding
+                         is torch's float8_e4m3fn conversion, pinned against CUDA's own
+                         conversion by tests/test_fp8_cpu.py
 Dtypes: "f16" inputs are np.float16 arrays; "f32" np.float32; "bf16" are np.float32 arrays
 holding bfloat16-representable values (numpy has no bfloat16).
 """
@@ -104,6 +109,38 @@ def dequantize_kv(k_cache, v_cache, k_scales, v_scales):
     """fp32 K/V from int8 + per-token scales (paged_decode_attn.py:202-216)."""
     k = k_cache.astype(np.float32) * k_scales[:, :, None, :, None]
     v = v_cache.astype(np.float32) * v_scales[:, :, None, :]
+    return k, v
+
+
+FP8_MAX = 448.0  # largest finite e4m3 value
+
+
+def quantize_per_token_fp8(x):
+    """Per-token e4m3: scale = amax / 448 (fp32, IEEE divide), q = e4m3(x / scale) with
+    round-to-nearest-even and saturation to +-448; zero rows give scale 0 and zeros. Returns
+    (q as uint8 e4m3 bit patterns, fp32 scales over all but the last axis)."""
+    import torch
+    xf = np.asarray(x, dtype=np.float32)
+    amax = np.abs(xf).max(axis=-1)
+    scale = (amax / np.float32(FP8_MAX)).astype(np.float32)
+    safe = np.where(scale > 0, scale, np.float32(1)).astype(np.float32)
+    y = np.clip(xf / safe[..., None], -FP8_MAX, FP8_MAX).astype(np.float32)
+    q = torch.from_numpy(np.ascontiguousarray(y)).to(torch.float8_e4m3fn).view(torch.uint8)
+    q = np.where(scale[..., None] > 0, q.numpy(), 0).astype(np.uint8)
+    return q, scale
+
+
+def fp8_to_float(q_u8):
+    """float32 values of uint8 e4m3 bit patterns."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(q_u8, dtype=np.uint8)).view(torch.float8_e4m3fn)
+    return t.float().numpy()
+
+
+def dequantize_fp8(k_cache, v_cache, k_scales, v_scales):
+    """fp32 K/V from an e4m3 (uint8 bit patterns) paged cache + per-token scales."""
+    k = fp8_to_float(k_cache) * k_scales[:, :, None, :, None]
+    v = fp8_to_float(v_cache) * v_scales[:, :, None, :]
     return k, v
 
 
