@@ -40,7 +40,7 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
+    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6])
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--splitk", action="store_true", help="use the split-K pair")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -90,7 +90,7 @@ def build_workload(torch, cfg, rank, world, device):
         B, H, KVH, int8 = 64, 32, 8, False
         lens = np.full(B, 4096, dtype=np.int64)
         NB = 16384
-    elif cfg == 3:
+    elif cfg in (3, 6):
         B, H, KVH, int8 = 64, 12, 2, True
         lens = np.full(B, 8192 - 1, dtype=np.int64)  # +1 token written each step
         NB = B * 8192 // BLOCK + 64
@@ -111,7 +111,8 @@ def build_workload(torch, cfg, rank, world, device):
         B = len(lens)
         NB = int(sum((int(c) + 1 + BLOCK - 1) // BLOCK for c in lens)) * 2 + 64
     w.B, w.H, w.KVH, w.int8, w.NB = B, H, KVH, int8, NB
-    w.step_tokens = 1 if cfg in (3, 5) else 0
+    w.fp8 = cfg == 6  # config 3's shapes with the FP8 (e4m3) cache instead of INT8
+    w.step_tokens = 1 if cfg in (3, 5, 6) else 0
     w.lens_host = lens.astype(np.int32)
     maxb = int((lens.max() + w.step_tokens + BLOCK - 1) // BLOCK)
     # Fragmented pool: every sequence's blocks come from one seeded permutation of the pool.
@@ -126,7 +127,7 @@ def build_workload(torch, cfg, rank, world, device):
     w.context_lens = torch.from_numpy(w.lens_host + w.step_tokens).to(device)
     w.q = torch.randn(B, H, HEAD_DIM, generator=gen, device=device).to(torch.float16)
     w.out = torch.empty_like(w.q)
-    dt = torch.int8 if int8 else torch.float16
+    dt = torch.float8_e4m3fn if w.fp8 else (torch.int8 if int8 else torch.float16)
     w.k_cache = torch.empty(NB, KVH, HEAD_DIM // 8, BLOCK, 8, dtype=dt, device=device)
     w.v_cache = torch.empty(NB, KVH, HEAD_DIM, BLOCK, dtype=dt, device=device)
     if not int8:
@@ -143,9 +144,20 @@ def build_workload(torch, cfg, rank, world, device):
             L = int(lens[b0:b1].max())
             k = _kv_rows(torch, (b1 - b0, L, KVH, HEAD_DIM), "lognormal_outlier", gen, device)
             v = _kv_rows(torch, (b1 - b0, L, KVH, HEAD_DIM), "lognormal_outlier", gen, device)
-            ops.prefill_into_cache(k, v, w.k_cache, w.v_cache, bt[b0:b1].contiguous(),
-                                   torch.from_numpy(w.lens_host[b0:b1]).to(device), BLOCK,
-                                   k_scales=w.k_scales, v_scales=w.v_scales)
+            if w.fp8:
+                # Token rows through the FP8 write kernel (slot -1 past each context).
+                t = torch.arange(L, device=device)
+                lens_c = torch.from_numpy(w.lens_host[b0:b1].astype(np.int64)).to(device)
+                blk = bt[b0:b1].long().gather(1, (t // BLOCK).expand(b1 - b0, L))
+                slots = torch.where(t[None, :] < lens_c[:, None], blk * BLOCK + t % BLOCK,
+                                    torch.full_like(blk, -1)).to(torch.int32).reshape(-1)
+                ops.quantize_into_cache(k.reshape(-1, KVH, HEAD_DIM), v.reshape(-1, KVH, HEAD_DIM),
+                                        w.k_cache, w.v_cache, w.k_scales, w.v_scales, slots,
+                                        BLOCK)
+            else:
+                ops.prefill_into_cache(k, v, w.k_cache, w.v_cache, bt[b0:b1].contiguous(),
+                                       torch.from_numpy(w.lens_host[b0:b1]).to(device), BLOCK,
+                                       k_scales=w.k_scales, v_scales=w.v_scales)
             del k, v
     if w.step_tokens:
         # The token written each step: slot of position lens[b] in sequence b.
@@ -312,14 +324,16 @@ def config_desc(cfg, w, splitk):
     names = {2: "cfg2 FP16 decode B64 ctx4096 32/8 heads",
              3: "cfg3 INT8 per-token decode + 1-token quantize-write B64 ctx8192 12/2",
              4: "cfg4 INT8 split-K decode B8 ctx U[65536,131072] 64/8 (kv-head sharded)",
-             5: "cfg5 ragged INT8 serving B256 28/4 + 1-token write (sequence sharded)"}
+             5: "cfg5 ragged INT8 serving B256 28/4 + 1-token write (sequence sharded)",
+             6: "cfg6 FP8-e4m3 per-token decode + 1-token quantize-write B64 ctx8192 12/2"}
     d = {"workload": names[cfg], "head_dim": HEAD_DIM, "block_size": BLOCK,
          "op": ("splitk pair" if (splitk or cfg == 4) else "single-pass"),
          "l2": "inputs larger than L2 (126 MB): KV cache %.0f MB per GPU" % (w.cache_bytes / 1e6)
          if w is not None else "n/a"}
     if w is not None:
         d.update({"global_batch": None, "per_gpu_batch": w.B, "num_heads": w.H,
-                  "num_kv_heads": w.KVH, "kv_dtype": "int8" if w.int8 else "fp16",
+                  "num_kv_heads": w.KVH,
+                  "kv_dtype": "fp8_e4m3" if w.fp8 else ("int8" if w.int8 else "fp16"),
                   "ctx_tokens_per_gpu": w.ctx_total})
     return d
 
@@ -443,7 +457,11 @@ def main():
             if w.step_tokens:
                 ops.quantize_into_cache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.k_scales,
                                         w.v_scales, w.slots, BLOCK)
-            if w.int8:
+            if w.fp8:
+                # No reference op takes an FP8 cache: the library's own decode op.
+                ops.decode(dout, dq, w.k_cache, w.v_cache, dbt, dcl, scale, BLOCK,
+                           k_scales=w.k_scales, v_scales=w.v_scales, splitk=args.splitk)
+            elif w.int8:
                 name = "splitk_int8" if (args.splitk or args.config == 4) else "warp_int8"
                 cuda_ext.VARIANTS_INT8[name](dout, dq, w.k_cache, w.v_cache, w.k_scales,
                                              w.v_scales, dbt, dcl, scale, BLOCK)
@@ -470,7 +488,8 @@ def main():
         e2e = {"value": total_bytes / e2e_s / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "seqs_per_s": total_seqs / e2e_s, "ms_per_step": e2e_s * 1e3,
-               "path": "pa_b200.cuda_ext (validate=True: one context_lens host check/step)"}
+               "path": ("pa_b200.ops.decode" if w.fp8 else "pa_b200.cuda_ext") +
+                       " (validate=True: one context_lens host check/step)"}
 
     peak, peak_kind = measured_peak()
     value = total_bytes / (ms * 1e-3) / 1e9
@@ -479,7 +498,8 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8" if w.int8 else "f16", "data": "synthetic",
+        "vs_baseline": None, "dtype": "fp8_e4m3" if w.fp8 else ("int8" if w.int8 else "f16"),
+        "data": "synthetic",
         "config": config_desc(args.config, w, args.splitk),
         "seqs_per_s": total_seqs / (ms * 1e-3),
         "pct_of_nominal_8000": 100.0 * per_gpu / NOMINAL_GBS,
