@@ -8,13 +8,13 @@
  * aborts, traps or synchronises the device, except pa_read_status().
  *
  * Paged KV layout (the reference's, tests/paged_decode_attn.py:6-7,76-81,156-164):
- *   k_cache  [num_blocks, num_kv_heads, head_dim/8, block_size, 8]   fp16 or int8
- *   v_cache  [num_blocks, num_kv_heads, head_dim,   block_size]      fp16 or int8
- *   k_scales [num_blocks, num_kv_heads, block_size] fp32  (int8 cache only)
+ *   k_cache  [num_blocks, num_kv_heads, head_dim/8, block_size, 8]   fp16, int8 or fp8 e4m3
+ *   v_cache  [num_blocks, num_kv_heads, head_dim,   block_size]      fp16, int8 or fp8 e4m3
+ *   k_scales [num_blocks, num_kv_heads, block_size] fp32  (int8 and fp8 caches)
  *   v_scales [num_blocks, num_kv_heads, block_size] fp32
  *   block_table  [num_seqs, max_blocks_per_seq] int32
  *   context_lens [num_seqs] int32
- *   q, out [num_seqs, num_heads, head_dim] fp16
+ *   q, out [num_seqs, num_heads, head_dim] fp16 (bf16 with pa_decode_bf16q)
  * Supported: head_dim 128, block_size a multiple of 16 dividing 128, x = 8, num_heads a
  * multiple of num_kv_heads.
  *
