@@ -1225,7 +1225,7 @@ template <> struct Shape<1, 8> { static constexpr int W = PA_I8_WARPS, DP = PA_I
 template <> struct Shape<0, 8> { static constexpr int W = PA_F16_WARPS, DP = PA_F16_DEPTH; };
 template <> struct Shape<1, 16> { static constexpr int W = 8, DP = 4; };
 template <> struct Shape<0, 16> { static constexpr int W = 8, DP = 3; };
-template <> struct Shape<2, 8> { static constexpr int W = 8, DP = 4; };
+template <> struct Shape<2, 8> { static constexpr int W = 12, DP = 3; };
 template <> struct Shape<2, 16> { static constexpr int W = 8, DP = 4; };
 
 template <int KVK, int GT>
