@@ -250,8 +250,9 @@ __device__ __forceinline__ void i8x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32
 __device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
   const __half2_raw a = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xffffu), __NV_E4M3);
   const __half2_raw b = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
-  lo = (uint32_t)a.x | ((uint32_t)a.y << 16);
-  hi = (uint32_t)b.x | ((uint32_t)b.y << 16);
+  // __half2_raw is {x, y} in memory order: as one 32-bit word, x is the low half.
+  lo = *reinterpret_cast<const uint32_t*>(&a);
+  hi = *reinterpret_cast<const uint32_t*>(&b);
 }
 
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
