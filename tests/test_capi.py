@@ -75,3 +75,33 @@ def test_host_argument_checks(lib):
     assert rc == _lib.PA_ERR_UNSUPPORTED
     rc = lib.pa_absmax_scale(1 << 20, 0, 10, 1 << 20, 7, 1 << 20, None)
     assert rc == _lib.PA_ERR_INVALID_ARG
+
+
+def test_extension_entry_points_check_arguments_on_the_host(lib):
+    names = set(_declared())
+    for must in ("pa_decode_fp8", "pa_splitk_fp8", "pa_quantize_into_cache_fp8",
+                 "pa_decode_bf16q", "pa_decode_bf16q_workspace_bytes",
+                 "pa_selftest_bounded_wait", "pa_decode_f16_noalloc"):
+        assert must in names
+    assert b"fp16 range" in lib.pa_status_string(_lib.PA_ERR_Q_RANGE)
+    p = 1 << 20
+    # bf16 activations: only fp16 / int8 / fp8 caches
+    rc = lib.pa_decode_bf16q(p, p, p, p, p, p, p, p, 1, 8, 2, 128, 4, 16, 2, _lib.PA_DTYPE_F32, 0,
+                             0.1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_UNSUPPORTED and b"kv_dtype" in lib.pa_last_error()
+    rc = lib.pa_decode_bf16q(p, p, p, p, p, p, p, p, 1, 7, 2, 128, 4, 16, 2, _lib.PA_DTYPE_F16, 0,
+                             0.1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_INVALID_ARG
+    # fp8 decode: the same shape rules as the other decode ops
+    rc = lib.pa_decode_fp8(p, p, p, p, p, p, p, p, 1, 8, 2, 64, 4, 16, 2, 0.1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_UNSUPPORTED
+    rc = lib.pa_splitk_fp8(p, p, p, p, p, p, p, p, 1, 8, 2, 128, 4, 24, 2, 0.1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_INVALID_ARG
+    # fp8 write: input dtype and null pointers
+    rc = lib.pa_quantize_into_cache_fp8(p, p, 9, 256, p, 4, 2, 128, p, p, p, p, 4, 16, None, None)
+    assert rc == _lib.PA_ERR_UNSUPPORTED
+    rc = lib.pa_quantize_into_cache_fp8(p, p, _lib.PA_DTYPE_F16, 256, p, 4, 2, 128, p, p, None, p,
+                                        4, 16, None, None)
+    assert rc == _lib.PA_ERR_INVALID_ARG
+    # the wait self-test needs a status word
+    assert lib.pa_selftest_bounded_wait(None, None) == _lib.PA_ERR_INVALID_ARG
