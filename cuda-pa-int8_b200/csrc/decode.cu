@@ -1,11 +1,13 @@
-// Paged-attention decode kernels for B200 (sm_100a): FP16 and per-token INT8 KV caches.
+// Paged-attention decode kernels for B200 (sm_100a): FP16, per-token INT8 and per-token FP8
+// (e4m3) KV caches.
 //
 // Design (one kernel family, three modes, see pa_internal.h):
 //  * A warp is an independent decode engine. It owns a DEPTH-deep ring of shared-memory
 //    stages; its lane 0 fills them with TMA copies (the K tile through a tensor map with the
 //    128-byte swizzle, V and the per-token scales through 1-D bulk copies or tensor maps) and
 //    the whole warp consumes them. A stage holds one 16-token "subpage" of one
-//    (block, kv-head) page: K and V tiles plus, for INT8, 16 K scales and 16 V scales.
+//    (block, kv-head) page: K and V tiles plus, for INT8 and FP8, 16 K scales and 16 V
+//    scales. The ranges are walked piece by piece (a warp's pages inside one segment).
 //  * Every CTA first scans context_lens (all sequences, kept in shared memory) and then the
 //    flattened work list "sequence x kv-head x head-tile x subpage" is cut into equal page
 //    ranges, one per warp (stream mode), so ragged batches and long contexts are balanced.
@@ -16,10 +18,13 @@
 //    (the split-K pair); partial mode writes one merged partial per segment (cross-GPU).
 //  * All q heads of a GQA group share one pass over the K/V page: QK^T and PV run on the
 //    tensor cores (mma.sync m16n8k16, f16 in / f32 accumulate) with heads on the MMA rows
-//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8 K/V bytes are
-//    unpacked to exact fp16 integers in registers; the per-token K scale multiplies the
-//    integer dot product and the per-token V scale is folded into the softmax weight
-//    (the dequant fusion of kernels/paged_attention_v5_warp_int8.cu:82-85,101-108).
+//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8: QK runs on
+//    the integer tensor cores (m16n8k32) on the raw K bytes against q split into two int8
+//    parts; V bytes are unpacked to exact fp16 integers in registers. FP8: K and V bytes
+//    convert to fp16 exactly in registers (hardware e4m3x2 -> f16x2). For both, the
+//    per-token K scale multiplies the dot product and the per-token V scale is folded into
+//    the softmax weight (the dequant fusion of kernels/paged_attention_v5_warp_int8.cu:
+//    82-85,101-108).
 //
 // Arithmetic follows the reference decode (tests/paged_decode_attn.py:4-49 and the split-K
 // pair kernels/paged_attention_v4_splitk.cu:28-187): softmax(scale * q.k) v over the tokens

@@ -1,11 +1,11 @@
 // Shared device helpers for the B200 paged-attention decode path.
 //
 // Everything here is sm_100a device code written for this library: thin inline-PTX wrappers
-// for mbarriers, TMA bulk / tensor copies and the m16n8k16 f16 MMA, plus the int8 -> fp16
-// unpack used to feed quantized K/V pages to the tensor cores.
+// for mbarriers, TMA bulk / tensor copies and the f16 / s8 MMAs, plus the int8 -> fp16 unpack
+// and the e4m3 -> fp16 conversion used to feed quantized K/V pages to the tensor cores.
 //
 // Paged KV layout (identical to the reference's, tests/paged_decode_attn.py:6-7,76-81):
-//   K  [num_blocks, kv_heads, D/8, block_size, 8]   (fp16 or int8, x = 8)
+//   K  [num_blocks, kv_heads, D/8, block_size, 8]   (fp16, int8 or e4m3, x = 8)
 //   V  [num_blocks, kv_heads, D,   block_size]
 //   Ks/Vs [num_blocks, kv_heads, block_size] fp32 (int8 cache only)
 #pragma once
