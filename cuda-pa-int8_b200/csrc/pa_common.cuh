@@ -7,7 +7,7 @@
 // Paged KV layout (identical to the reference's, tests/paged_decode_attn.py:6-7,76-81):
 //   K  [num_blocks, kv_heads, D/8, block_size, 8]   (fp16, int8 or e4m3, x = 8)
 //   V  [num_blocks, kv_heads, D,   block_size]
-//   Ks/Vs [num_blocks, kv_heads, block_size] fp32 (int8 cache only)
+//   Ks/Vs [num_blocks, kv_heads, block_size] fp32 (int8 and e4m3 caches)
 #pragma once
 
 #include <cuda.h>
