@@ -32,14 +32,15 @@ _OPT_OPS_INT8 = {
 
 def paged_decode_attention(out, q, k_cache, v_cache, block_table, context_lens, scale,
                            block_size=16):
-    _ops.decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size)
+    _ops.decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size,
+                kv_kind="f16")
     return out
 
 
 def _make_variant(op_name, splitk):
     def run(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16):
         _ops.decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size,
-                    splitk=splitk)
+                    splitk=splitk, kv_kind="f16")
         return out
     run.__name__ = op_name
     return run
@@ -49,7 +50,7 @@ def _make_variant_int8(op_name, splitk):
     def run(out, q, k_cache, v_cache, k_scales, v_scales, block_table, context_lens, scale,
             block_size=16):
         _ops.decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size,
-                    k_scales=k_scales, v_scales=v_scales, splitk=splitk)
+                    k_scales=k_scales, v_scales=v_scales, splitk=splitk, kv_kind="i8")
         return out
     run.__name__ = op_name
     return run

@@ -173,15 +173,17 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
 
 
 def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
-           k_scales=None, v_scales=None, splitk=False, validate=True):
+           k_scales=None, v_scales=None, splitk=False, validate=True, kv_kind=None):
     """Paged decode attention into `out` (fp16 [num_seqs, num_heads, head_dim]).
 
     FP16 cache when k_scales is None, otherwise INT8 with per-token fp32 scales. splitk
     selects the partition + LSE-reduce kernel pair (512-token splits); otherwise the
     single-pass kernel with the fused combine runs. validate=False skips the one host sync
     that checks context_lens (the kernels still flag bad lengths in the status word).
+    kv_kind ('f16', 'i8' or 'f8') pins the cache type instead of inferring it from the
+    tensors, so a cache of another type is rejected (the reference-named ops use this).
     """
-    kind = _kv_kind(k_cache, k_scales)
+    kind = kv_kind or _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
                                           block_size, kind, k_scales, v_scales, validate)
     if B == 0:

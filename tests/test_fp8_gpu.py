@@ -104,3 +104,18 @@ def test_fp8_cache_write_is_bit_exact(in_dtype):
         assert np.array_equal(vcache[blk, :, :, off], vq[n])
         assert np.array_equal(kscale[blk, :, off], ks[n])
         assert np.array_equal(vscale[blk, :, off], vs[n])
+
+
+def test_reference_named_int8_ops_reject_an_fp8_cache():
+    """The drop-in names keep the reference's dtype contract: its INT8 ops take int8 caches
+    only, so an e4m3 cache is rejected there (it is decoded through ops.decode)."""
+    from pa_b200 import cuda_ext
+    c = fp16_case(83, 1, 8, 2, [40])
+    kc, vc, ks, vs = _fp8_case(c)
+    q, bt, cl, kss, vss = to_cuda(c["q"], c["block_table"], c["context_lens"], ks, vs)
+    with pytest.raises(RuntimeError, match="k_cache must be int8"):
+        cuda_ext.VARIANTS_INT8["warp_int8"](torch.empty_like(q), q, _to_fp8(kc), _to_fp8(vc),
+                                            kss, vss, bt, cl, scale_for(), BLOCK_SIZE)
+    with pytest.raises(RuntimeError, match="k_cache must be fp16"):
+        cuda_ext.VARIANTS["warp"](torch.empty_like(q), q, _to_fp8(kc), _to_fp8(vc), bt, cl,
+                                  scale_for(), BLOCK_SIZE)
