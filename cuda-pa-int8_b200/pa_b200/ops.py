@@ -111,7 +111,7 @@ _KV_CODE = {"f16": _lib.PA_DTYPE_F16, "i8": _lib.PA_DTYPE_I8, "f8": _lib.PA_DTYP
 def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
                        kind, k_scales, v_scales, validate, out_required=True,
                        act_dtype=torch.float16):
-    int8 = kind != "f16"  # one-byte cache with per-token scales (int8 or fp8)
+    scaled = kind != "f16"  # one-byte cache with per-token scales (int8 or fp8)
     _require(q.is_cuda and (out is None or out.is_cuda), "tensors must be on CUDA")
     act_name = "fp16" if act_dtype == torch.float16 else "bf16"
     _require(q.dtype == act_dtype, f"q must be {act_name}")
@@ -121,7 +121,7 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
     if kind == "i8":
         _require(k_cache.dtype == torch.int8, "k_cache must be int8")
         _require(v_cache.dtype == torch.int8, "v_cache must be int8")
-    if int8:
+    if scaled:
         _require(k_scales is not None and k_scales.dtype == torch.float32,
                  "k_scales must be fp32")
         _require(v_scales is not None and v_scales.dtype == torch.float32,
@@ -133,7 +133,7 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
     _require(context_lens.dtype == torch.int32, "context_lens must be int32")
     dev = q.device
     tensors = [k_cache, v_cache, block_table, context_lens] + ([out] if out is not None else [])
-    if int8:
+    if scaled:
         tensors += [k_scales, v_scales]
     for t in tensors:
         _require(t.device == dev, "all tensors must be on the same CUDA device")
@@ -145,7 +145,7 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
                  f"out must be {act_name} with the shape of q")
     _require(k_cache.dim() == 5, "k_cache must be [num_blocks, kv_heads, head_dim/x, block_size, x]")
     NB, KVH, DX, BS, x = k_cache.shape
-    if int8:
+    if scaled:
         _require(x == 8, "int8 K cache requires x == 8")
     _require(x == X, "K cache requires x == 8")
     _require(D == HEAD_DIM, f"head_dim {D} unsupported (this build: {HEAD_DIM})")
@@ -155,7 +155,7 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
     _require(BS == block_size, f"k_cache block dimension {BS} != block_size {block_size}")
     _require(tuple(v_cache.shape) == (NB, KVH, D, block_size),
              "v_cache must be [num_blocks, kv_heads, head_dim, block_size]")
-    if int8:
+    if scaled:
         _require(tuple(k_scales.shape) == (NB, KVH, block_size) and
                  tuple(v_scales.shape) == (NB, KVH, block_size),
                  "scales must be [num_blocks, kv_heads, block_size]")
