@@ -185,6 +185,13 @@ int check_common(int B, int H, int KVH, int D, int NB, int bs, int max_blocks) {
     return fail(PA_ERR_INVALID_ARG, "num_heads (%d) must be a multiple of num_kv_heads (%d)", H,
                 KVH);
   if (D != 128) return fail(PA_ERR_UNSUPPORTED, "head_dim %d unsupported (this build: 128)", D);
+  // The kernel's copy producer packs (page row << 3 | subpage) into an int, where
+  // page row = block * num_kv_heads + kv_head: 2^28 page rows (1 TB of fp16 K pages).
+  if ((long long)NB * KVH >= (1LL << 28))
+    return fail(PA_ERR_UNSUPPORTED,
+                "num_blocks * num_kv_heads = %lld page rows; this build addresses fewer than "
+                "2^28",
+                (long long)NB * KVH);
   if (bs % 16 != 0 || 128 % bs != 0)
     return fail(PA_ERR_INVALID_ARG,
                 "block_size must divide TILE (multiple of 16); got %d (supported: 16, 32, 64, "

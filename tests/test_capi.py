@@ -69,6 +69,8 @@ def test_host_argument_checks(lib):
     assert b"block_size" in lib.pa_last_error()
     assert _decode_f16(lib, bs=48) == _lib.PA_ERR_INVALID_ARG
     assert _decode_f16(lib, KVH=0) == _lib.PA_ERR_INVALID_ARG
+    assert _decode_f16(lib, NB=1 << 26, KVH=4) == _lib.PA_ERR_UNSUPPORTED  # 2^28 page rows
+    assert b"page rows" in lib.pa_last_error()
     assert _decode_f16(lib, B=0) == _lib.PA_OK  # empty batch: nothing to do
     rc = lib.pa_quantize_into_cache(1 << 20, 1 << 20, 9, 256, 1 << 20, 4, 2, 128, 1 << 20,
                                     1 << 20, 1 << 20, 1 << 20, 4, 16, None, None, None, None)
