@@ -132,7 +132,9 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
     _require(block_table.dtype == torch.int32, "block_table must be int32")
     _require(context_lens.dtype == torch.int32, "context_lens must be int32")
     dev = q.device
-    tensors = [k_cache, v_cache, block_table, context_lens] + ([out] if out is not None else [])
+    tensors = [q, k_cache, v_cache, block_table, context_lens]
+    if out is not None:
+        tensors.append(out)
     if scaled:
         tensors += [k_scales, v_scales]
     for t in tensors:
@@ -143,7 +145,8 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
     if out is not None:
         _require(tuple(out.shape) == (B, H, D) and out.dtype == act_dtype,
                  f"out must be {act_name} with the shape of q")
-    _require(k_cache.dim() == 5, "k_cache must be [num_blocks, kv_heads, head_dim/x, block_size, x]")
+    _require(k_cache.dim() == 5,
+             "k_cache must be [num_blocks, kv_heads, head_dim/x, block_size, x]")
     NB, KVH, DX, BS, x = k_cache.shape
     if scaled:
         _require(x == 8, "int8 K cache requires x == 8")
@@ -308,6 +311,30 @@ def merge_partials(out, partials, num_heads, num_kv_heads):
 # ---------------------------------------------------------------------------------------
 # Cache writes
 # ---------------------------------------------------------------------------------------
+def _check_cache_layout(k_cache, v_cache, num_kv_heads, head_dim, block_size, k_scales=None,
+                        v_scales=None):
+    """The paged layout the write kernels address, given the rows' kv-head count and head_dim:
+    K [num_blocks, kv_heads, head_dim/8, block_size, 8], V [num_blocks, kv_heads, head_dim,
+    block_size], scales [num_blocks, kv_heads, block_size] (tests/paged_decode_attn.py:76-81,
+    156-164). The kernels take only num_blocks and block_size, so any other shape would be
+    written out of bounds; it is rejected here. Returns num_blocks."""
+    _require(k_cache.dim() == 5,
+             "k_cache must be [num_blocks, kv_heads, head_dim/x, block_size, x]")
+    NB = k_cache.shape[0]
+    _require(head_dim % X == 0 and tuple(k_cache.shape) == (NB, num_kv_heads, head_dim // X,
+                                                             block_size, X),
+             f"k_cache must be [num_blocks, {num_kv_heads}, {head_dim // X}, {block_size}, {X}] "
+             f"for these rows; got {tuple(k_cache.shape)}")
+    _require(tuple(v_cache.shape) == (NB, num_kv_heads, head_dim, block_size),
+             f"v_cache must be [{NB}, {num_kv_heads}, {head_dim}, {block_size}]; "
+             f"got {tuple(v_cache.shape)}")
+    for name, t in (("k_scales", k_scales), ("v_scales", v_scales)):
+        if t is not None:
+            _require(tuple(t.shape) == (NB, num_kv_heads, block_size),
+                     f"{name} must be [{NB}, {num_kv_heads}, {block_size}]; got {tuple(t.shape)}")
+    return NB
+
+
 def _check_rows(key, value):
     _require(key.is_cuda and value.is_cuda, "tensors must be on CUDA")
     _require(key.dtype in _DTYPE_CODE and value.dtype == key.dtype,
@@ -343,8 +370,7 @@ def quantize_into_cache(key, value, k_cache, v_cache, k_scales, v_scales, slot_m
              "slot_mapping must be int32 on CUDA")
     N, KVH, D = key.shape
     _require(slot_mapping.numel() == N, "slot_mapping must have one entry per token")
-    _require(k_cache.shape[1] == KVH and k_cache.shape[3] == block_size,
-             "cache kv_heads/block_size mismatch")
+    _check_cache_layout(k_cache, v_cache, KVH, D, block_size, k_scales, v_scales)
     for t in (k_cache, v_cache, k_scales, v_scales, slot_mapping):
         _require(t.is_contiguous() and t.device == key.device,
                  "cache tensors must be contiguous and on the key's device")
@@ -379,8 +405,7 @@ def write_into_cache(key, value, k_cache, v_cache, slot_mapping, block_size=16):
              "slot_mapping must be int32 on CUDA")
     N, KVH, D = key.shape
     _require(slot_mapping.numel() == N, "slot_mapping must have one entry per token")
-    _require(k_cache.shape[1] == KVH and k_cache.shape[3] == block_size,
-             "cache kv_heads/block_size mismatch")
+    _check_cache_layout(k_cache, v_cache, KVH, D, block_size)
     for t in (k_cache, v_cache, slot_mapping):
         _require(t.is_contiguous() and t.device == key.device,
                  "cache tensors must be contiguous and on the key's device")
@@ -414,6 +439,8 @@ def prefill_into_cache(k, v, k_cache, v_cache, block_table, context_lens, block_
     if int8:
         _require(k_scales is not None and v_scales is not None, "int8 cache needs scales")
         tensors += [k_scales, v_scales]
+    _check_cache_layout(k_cache, v_cache, KVH, D, block_size, k_scales if int8 else None,
+                        v_scales if int8 else None)
     for t in tensors:
         _require(t.is_contiguous() and t.device == k.device,
                  "cache tensors must be contiguous and on k's device")

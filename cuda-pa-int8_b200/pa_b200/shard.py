@@ -8,7 +8,8 @@ Decode shards with no data exchange in two ways:
 Only when one sequence's context is split across GPUs is there an exchange: each rank
 computes un-normalised partials (O, m, l) for its token range (ops.decode_partial), the
 partials are all-gathered over NCCL (a few hundred KB), and every rank merges them with the
-log-sum-exp rule (ops.merge_partials). No kernel reads another GPU's memory: remote data arrives through NCCL.
+log-sum-exp rule (ops.merge_partials). No kernel reads another GPU's memory: remote data
+arrives through NCCL.
 """
 
 import heapq
