@@ -16,7 +16,7 @@
  *   context_lens [num_seqs] int32
  *   q, out [num_seqs, num_heads, head_dim] fp16 (bf16 with pa_decode_bf16q)
  * Supported: head_dim 128, block_size a multiple of 16 dividing 128, x = 8, num_heads a
- * multiple of num_kv_heads.
+ * multiple of num_kv_heads, num_blocks * num_kv_heads below 2^28 page rows.
  *
  * Workspace: the decode entry points need a device workspace of
  * pa_decode_workspace_bytes(...) bytes, zero-filled once before its first use (for example
@@ -68,8 +68,8 @@ const char* pa_last_error(void);
 const char* pa_status_string(int status);
 
 /* ------------------------------------------------------------------------------------
- * Decode workspace size for one call shape on the current device. kv_dtype is PA_DTYPE_F16
- * or PA_DTYPE_I8; splitk selects the split-K partition/reduce pair (nonzero) or the
+ * Decode workspace size for one call shape on the current device (0 for an unsupported
+ * shape). kv_dtype is PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3; splitk selects the split-K partition/reduce pair (nonzero) or the
  * single-pass op (zero).
  * ---------------------------------------------------------------------------------- */
 size_t pa_decode_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, int head_dim,
