@@ -220,7 +220,8 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
 
 def decode_bf16(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
                 k_scales=None, v_scales=None, splitk=False, validate=True):
-    """decode() with bf16 activations: q and out are bf16, the cache fp16 or per-token INT8.
+    """decode() with bf16 activations: q and out are bf16, the cache fp16, per-token INT8 or
+    per-token FP8 (e4m3).
 
     q is converted to fp16 on the device (exact for magnitudes in the fp16 normal range; larger
     values saturate and set the PA_ERR_Q_RANGE status bit), the fp16 decode runs, and the output

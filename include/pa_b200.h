@@ -118,14 +118,6 @@ int pa_splitk_i8(void* out, const void* q, const void* k_cache, const void* v_ca
                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                  float scale, void* workspace, size_t workspace_bytes, void* stream);
 
-/* FP16 single-pass decode that allocates nothing and takes no workspace, for callers that
- * cannot allocate device memory when they run attention: plugins whose host framework owns
- * all device memory, and serving loops that must stay out of any allocator. Its scratch is a
- * 12 MiB static device array that every GPU loading this code keeps until the process exits;
- * shapes whose scratch exceeds it (more than 8 q heads per kv head) are rejected with
- * PA_ERR_WORKSPACE. The first call on a device looks up the array's address and should come
- * before any stream capture. Calls share the array: calls that overlap on the GPU race, so
- * order them on one stream. This entry point has no counterpart in the reference. */
 /* FP8 (e4m3) KV cache: the INT8 page layout with e4m3 bytes and per-token fp32 scales
  * (value = e4m3 * scale; see pa_quantize_into_cache_fp8). Same arguments as pa_decode_i8 /
  * pa_splitk_i8. The reference lists an FP8 KV variant as future work
@@ -141,23 +133,22 @@ int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_c
                   int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                   float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* FP16 single-pass decode that allocates nothing and takes no workspace, for callers that
+ * cannot allocate device memory when they run attention: plugins whose host framework owns
+ * all device memory, and serving loops that must stay out of any allocator. Its scratch is a
+ * 12 MiB static device array that every GPU loading this code keeps until the process exits;
+ * shapes whose scratch exceeds it (more than 8 q heads per kv head) are rejected with
+ * PA_ERR_WORKSPACE. The first call on a device looks up the array's address and should come
+ * before any stream capture. Calls share the array: calls that overlap on the GPU race, so
+ * order them on one stream. This entry point has no counterpart in the reference. */
 int pa_decode_f16_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
                           const int32_t* block_table, const int32_t* context_lens, int num_seqs,
                           int num_heads, int num_kv_heads, int head_dim, int num_blocks,
                           int block_size, int max_blocks_per_seq, float scale, void* stream);
 
-/* ------------------------------------------------------------------------------------
- * Per-sequence partial decode for split-K across GPUs: like pa_decode_*, but instead of
- * the normalised fp16 output it writes, per (sequence, kv-head), an un-normalised partial
- * to `partials` (layout: [num_seqs*num_kv_heads][pa_partial_floats(...)] fp32; within a
- * slot O[head_dim][heads_per_slot] then m[heads_per_slot] then l[heads_per_slot], m in
- * log2 units). A sequence with context 0 yields an empty partial (m=-inf, l=0).
- * Generalises the partition kernel of kernels/paged_attention_v4_splitk.cu:28-153 from a
- * token split inside one GPU to a token range owned by one GPU.
- * ---------------------------------------------------------------------------------- */
 /* Decode with bf16 activations: q and out are bf16 [num_seqs, num_heads, head_dim]; the cache
- * is fp16 (kv_dtype PA_DTYPE_F16) or per-token int8 (PA_DTYPE_I8, with k_scales/v_scales);
- * splitk selects the split-K pair. q is converted to fp16 on the device (exact for magnitudes
+ * is fp16 (kv_dtype PA_DTYPE_F16), per-token int8 (PA_DTYPE_I8) or per-token fp8 e4m3
+ * (PA_DTYPE_FP8E4M3), the last two with k_scales/v_scales; splitk selects the split-K pair. q is converted to fp16 on the device (exact for magnitudes
  * in the fp16 normal range; larger values saturate and set PA_ERR_Q_RANGE in the status word),
  * the fp16 decode runs, and its output is rounded once to bf16. The workspace holds the decode
  * workspace followed by the fp16 copies: size it with pa_decode_bf16q_workspace_bytes. This is
@@ -178,6 +169,15 @@ int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v
  * The context stays usable. No counterpart in the reference. */
 int pa_selftest_bounded_wait(void* workspace, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Per-sequence partial decode for split-K across GPUs: like pa_decode_*, but instead of
+ * the normalised fp16 output it writes, per (sequence, kv-head), an un-normalised partial
+ * to `partials` (layout: [num_seqs*num_kv_heads][pa_partial_floats(...)] fp32; within a
+ * slot O[head_dim][heads_per_slot] then m[heads_per_slot] then l[heads_per_slot], m in
+ * log2 units). A sequence with context 0 yields an empty partial (m=-inf, l=0).
+ * Generalises the partition kernel of kernels/paged_attention_v4_splitk.cu:28-153 from a
+ * token split inside one GPU to a token range owned by one GPU.
+ * ---------------------------------------------------------------------------------- */
 int pa_partial_floats(int num_heads, int num_kv_heads, int head_dim);
 int pa_decode_partial(int kv_dtype, float* partials, const void* q, const void* k_cache,
                       const void* v_cache, const float* k_scales, const float* v_scales,

@@ -4,6 +4,8 @@ and rejects bad arguments on the host (no GPU work is launched here)."""
 import ctypes
 import os
 import re
+import shutil
+import subprocess
 
 import pytest
 
@@ -107,3 +109,20 @@ def test_extension_entry_points_check_arguments_on_the_host(lib):
     assert rc == _lib.PA_ERR_INVALID_ARG
     # the wait self-test needs a status word
     assert lib.pa_selftest_bounded_wait(None, None) == _lib.PA_ERR_INVALID_ARG
+
+
+def test_plain_c_caller(lib, tmp_path):
+    """tests/c_abi_check.c, a C99 program that includes only include/pa_b200.h and links the
+    library, compiles with -Wall -Wextra -pedantic -Werror and passes its host-side checks."""
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "c_abi_check.c")
+    libdir = os.path.dirname(build.LIB_PATH)
+    exe = str(tmp_path / "c_abi_check")
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I",
+                    build.INCLUDE_DIR, src, "-L", libdir, "-lpa_b200", "-Wl,-rpath," + libdir,
+                    "-o", exe], check=True, capture_output=True, text=True)
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stderr
+    assert "c abi ok" in res.stdout

@@ -68,6 +68,24 @@ def test_fp8_decode_ignores_nan_bytes_past_the_context():
     assert_close(out, oracle_out(c["q"], kd, vd, c["block_table"], c["context_lens"]))
 
 
+@pytest.mark.parametrize("splitk", [False, True])
+def test_fp8_cache_with_bf16_q(splitk):
+    """bf16 q and out over an FP8 cache (pa_decode_bf16q with PA_DTYPE_FP8E4M3)."""
+    c = fp16_case(84, 3, 12, 2, [1, 600, 37])
+    kc, vc, ks, vs = _fp8_case(c)
+    qb = torch.from_numpy(np.ascontiguousarray(c["q"])).to(torch.bfloat16)
+    q = qb.cuda()
+    bt, cl, kss, vss = to_cuda(c["block_table"], c["context_lens"], ks, vs)
+    out = torch.empty_like(q)
+    _ops().decode_bf16(out, q, _to_fp8(kc), _to_fp8(vc), bt, cl, scale_for(), BLOCK_SIZE,
+                       k_scales=kss, v_scales=vss, splitk=splitk)
+    assert out.dtype == torch.bfloat16
+    kd, vd = pa_oracle.dequantize_fp8(kc, vc, ks, vs)
+    assert_close(out, oracle_out(qb.float().numpy(), kd, vd, c["block_table"],
+                                 c["context_lens"]))
+    _ops().check_status(q.device)
+
+
 @pytest.mark.parametrize("in_dtype", [torch.float16, torch.bfloat16, torch.float32])
 def test_fp8_cache_write_is_bit_exact(in_dtype):
     rng = np.random.default_rng(5)
