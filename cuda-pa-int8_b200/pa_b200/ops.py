@@ -9,7 +9,6 @@ zero-filled once when allocated and kept for later calls.
 """
 
 import ctypes
-import math
 
 import torch
 
@@ -109,8 +108,7 @@ _KV_CODE = {"f16": _lib.PA_DTYPE_F16, "i8": _lib.PA_DTYPE_I8, "f8": _lib.PA_DTYP
 
 
 def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
-                       kind, k_scales, v_scales, validate, out_required=True,
-                       act_dtype=torch.float16):
+                       kind, k_scales, v_scales, validate, act_dtype=torch.float16):
     scaled = kind != "f16"  # one-byte cache with per-token scales (int8 or fp8)
     _require(q.is_cuda and (out is None or out.is_cuda), "tensors must be on CUDA")
     act_name = "fp16" if act_dtype == torch.float16 else "bf16"

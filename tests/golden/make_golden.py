@@ -11,7 +11,6 @@ Reference functions exercised (all on CPU, torch):
   benchmarks/int8_bridge/paged_cache.py: PagedKVCache.prefill / decode_append
 """
 
-import math
 import os
 import sys
 

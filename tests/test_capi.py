@@ -1,7 +1,6 @@
 """CPU: the C-ABI library builds, loads, exports every function include/pa_b200.h declares,
 and rejects bad arguments on the host (no GPU work is launched here)."""
 
-import ctypes
 import os
 import re
 import shutil

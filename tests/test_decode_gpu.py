@@ -6,15 +6,14 @@ per-tensor against the dequantised-cache oracle, finite outputs, ctx=0 rejection
 precision metrics; tolerance tightened to the north-star 2e-3 abs / 1e-2 rel.
 """
 
-import math
 
 import numpy as np
 import pytest
 import torch
 
 import pa_oracle
-from pa_testlib import (BLOCK_SIZE, HEAD_DIM, assert_close, fp16_case, int8_case, make_lens,
-                        oracle_out, scale_for, to_cuda)
+from pa_testlib import (BLOCK_SIZE, assert_close, fp16_case, int8_case, make_lens, oracle_out,
+                        scale_for, to_cuda)
 
 pytestmark = pytest.mark.gpu
 

@@ -9,7 +9,6 @@ inputs, on two calls in a row: the second call reuses the array the first one le
 This file is collected last so that a run stopping at the first failure has run the others.
 """
 
-import numpy as np
 import pytest
 import torch
 
