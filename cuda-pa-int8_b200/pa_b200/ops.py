@@ -35,7 +35,10 @@ def _stream(device):
 
 
 def workspace(device, nbytes):
-    """The zero-initialised workspace of (device, current stream), grown to nbytes."""
+    """The zero-initialised workspace of (device, current stream), grown to nbytes.
+
+    Growing replaces the buffer, and a CUDA graph keeps the address it captured: run each
+    shape once before capturing it, so the graph records the final buffer."""
     stream = _stream(device)
     key = (device.index, stream)
     ws = _workspaces.get(key)
