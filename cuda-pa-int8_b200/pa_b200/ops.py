@@ -37,8 +37,9 @@ def _stream(device):
 def workspace(device, nbytes):
     """The zero-initialised workspace of (device, current stream), grown to nbytes.
 
-    Growing replaces the buffer, and a CUDA graph keeps the address it captured: run each
-    shape once before capturing it, so the graph records the final buffer."""
+    Growing replaces the buffer, and a CUDA graph keeps the address it captured: run the
+    largest shape once on a stream before capturing graphs on it, so no later call on that
+    stream replaces the buffer a graph uses."""
     stream = _stream(device)
     key = (device.index, stream)
     ws = _workspaces.get(key)
