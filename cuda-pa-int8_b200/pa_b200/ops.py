@@ -181,7 +181,8 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
            k_scales=None, v_scales=None, splitk=False, validate=True, kv_kind=None):
     """Paged decode attention into `out` (fp16 [num_seqs, num_heads, head_dim]).
 
-    FP16 cache when k_scales is None, otherwise INT8 with per-token fp32 scales. splitk
+    The cache type follows the tensors: fp16; int8 or float8_e4m3fn, each with per-token fp32
+    k_scales/v_scales (an int8 cache is assumed whenever scales are given). splitk
     selects the partition + LSE-reduce kernel pair (512-token splits); otherwise the
     single-pass kernel with the fused combine runs. validate=False skips the one host sync
     that checks context_lens (the kernels still flag bad lengths in the status word).
