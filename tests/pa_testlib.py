@@ -53,6 +53,53 @@ def int8_case(c, mode, block_size=BLOCK_SIZE):
     return dict(k_cache=kc, v_cache=vc, k_scales=kss, v_scales=vss)
 
 
+def ragged_case(seed, num_heads, num_kv_heads, lens, block_size=BLOCK_SIZE):
+    """A large ragged batch drawn token by token: N(0,1) fp16 q/K/V from numpy's seeded
+    generator, only for the valid tokens of each sequence, scattered straight into the paged
+    cache (no [num_seqs, max_len] padding, which for long-tailed lengths is most of the
+    memory). Also returns the fp16 rows per sequence for the INT8 variant (ragged_int8)."""
+    rng = np.random.default_rng(seed)
+    lens = np.asarray(lens, dtype=np.int32)
+    S, H, KVH, D = len(lens), num_heads, num_kv_heads, HEAD_DIM
+    nb = sum((int(n) + block_size - 1) // block_size for n in lens) + 1
+    bt = gen.block_table_for(gen.Gen(seed), lens, nb, block_size)
+    q = rng.standard_normal((S, H, D), dtype=np.float32).astype(np.float16)
+    kc = np.zeros((nb, KVH, D // 8, block_size, 8), np.float16)
+    vc = np.zeros((nb, KVH, D, block_size), np.float16)
+    rows = []
+    for b, n in enumerate(lens):
+        k = rng.standard_normal((int(n), KVH, D), dtype=np.float32).astype(np.float16)
+        v = rng.standard_normal((int(n), KVH, D), dtype=np.float32).astype(np.float16)
+        t = np.arange(int(n))
+        blk, off = bt[b, t // block_size], t % block_size
+        kc[blk, :, :, off, :] = k.reshape(int(n), KVH, D // 8, 8)
+        vc[blk, :, :, off] = v
+        rows.append((k, v))
+    return dict(q=q, k_cache=kc, v_cache=vc, block_table=bt, context_lens=lens, num_blocks=nb,
+                rows=rows)
+
+
+def ragged_int8(c, block_size=BLOCK_SIZE):
+    """Per-token INT8 cache of a ragged_case, quantised row by row with the oracle."""
+    nb, bt = c["num_blocks"], c["block_table"]
+    KVH, D = c["k_cache"].shape[1], HEAD_DIM
+    kc = np.zeros((nb, KVH, D // 8, block_size, 8), np.int8)
+    vc = np.zeros((nb, KVH, D, block_size), np.int8)
+    ks = np.zeros((nb, KVH, block_size), np.float32)
+    vs = np.zeros((nb, KVH, block_size), np.float32)
+    for b, (k, v) in enumerate(c["rows"]):
+        n = k.shape[0]
+        kq, ksc = pa_oracle.quantize_per_token(k, "f16")
+        vq, vsc = pa_oracle.quantize_per_token(v, "f16")
+        t = np.arange(n)
+        blk, off = bt[b, t // block_size], t % block_size
+        kc[blk, :, :, off, :] = kq.reshape(n, KVH, D // 8, 8)
+        vc[blk, :, :, off] = vq
+        ks[blk, :, off] = ksc
+        vs[blk, :, off] = vsc
+    return dict(k_cache=kc, v_cache=vc, k_scales=ks, v_scales=vs)
+
+
 def oracle_out(q, k_cache, v_cache, bt, lens, scale=None):
     return pa_oracle.paged_decode_attention(q, k_cache, v_cache, bt, lens, scale=scale)
 

@@ -13,7 +13,7 @@ import torch
 
 import pa_oracle
 from pa_testlib import (BLOCK_SIZE, assert_close, fp16_case, int8_case, make_lens, oracle_out,
-                        scale_for, to_cuda)
+                        ragged_case, ragged_int8, scale_for, to_cuda)
 
 pytestmark = pytest.mark.gpu
 
@@ -136,13 +136,13 @@ def test_ragged_batch_many_sequences(kind):
     cross-warp combine path is exercised heavily."""
     g = np.random.default_rng(5)
     lens = np.clip(np.exp(g.normal(np.log(300), 1.0, size=150)), 1, 5000).astype(int).tolist()
-    c = fp16_case(4, len(lens), 28, 4, lens)
+    c = ragged_case(4, 28, 4, lens)
     if kind == "fp16":
         out = _run_fp16("warp", c)
         ref = oracle_out(c["q"], c["k_cache"], c["v_cache"], c["block_table"],
                          c["context_lens"])
     else:
-        qc = int8_case(c, "per_token")
+        qc = ragged_int8(c)
         out = _run_int8("warp_int8", c, qc)
         ref = _int8_oracle(c, qc)
     assert_close(out, ref)
