@@ -53,11 +53,24 @@ def int8_case(c, mode, block_size=BLOCK_SIZE):
     return dict(k_cache=kc, v_cache=vc, k_scales=kss, v_scales=vss)
 
 
-def ragged_case(seed, num_heads, num_kv_heads, lens, block_size=BLOCK_SIZE):
-    """A large ragged batch drawn token by token: N(0,1) fp16 q/K/V from numpy's seeded
-    generator, only for the valid tokens of each sequence, scattered straight into the paged
-    cache (no [num_seqs, max_len] padding, which for long-tailed lengths is most of the
-    memory). Also returns the fp16 rows per sequence for the INT8 variant (ragged_int8)."""
+def _rows(rng, n, kvh, d, dist, outlier_ch):
+    """K or V rows [n, kvh, d]: N(0,1), or for "lognormal_outlier" each (token, kv-head) row
+    scaled by LogNormal(0, 0.5) and one fixed channel per kv-head x20 (oracle/gen.py's
+    stress distribution)."""
+    x = rng.standard_normal((n, kvh, d), dtype=np.float32)
+    if dist == "lognormal_outlier":
+        x *= np.exp(0.5 * rng.standard_normal((n, kvh, 1), dtype=np.float32))
+        x[:, np.arange(kvh), outlier_ch] *= 20.0
+    elif dist != "normal":
+        raise ValueError(dist)
+    return x.astype(np.float16)
+
+
+def ragged_case(seed, num_heads, num_kv_heads, lens, block_size=BLOCK_SIZE, dist="normal"):
+    """A large ragged batch drawn token by token: fp16 q/K/V from numpy's seeded generator,
+    only for the valid tokens of each sequence, scattered straight into the paged cache (no
+    [num_seqs, max_len] padding, which for long-tailed lengths is most of the memory). Also
+    returns the fp16 rows per sequence for the INT8 variant (ragged_int8)."""
     rng = np.random.default_rng(seed)
     lens = np.asarray(lens, dtype=np.int32)
     S, H, KVH, D = len(lens), num_heads, num_kv_heads, HEAD_DIM
@@ -67,9 +80,10 @@ def ragged_case(seed, num_heads, num_kv_heads, lens, block_size=BLOCK_SIZE):
     kc = np.zeros((nb, KVH, D // 8, block_size, 8), np.float16)
     vc = np.zeros((nb, KVH, D, block_size), np.float16)
     rows = []
+    ch_k, ch_v = rng.integers(0, D, KVH), rng.integers(0, D, KVH)
     for b, n in enumerate(lens):
-        k = rng.standard_normal((int(n), KVH, D), dtype=np.float32).astype(np.float16)
-        v = rng.standard_normal((int(n), KVH, D), dtype=np.float32).astype(np.float16)
+        k = _rows(rng, int(n), KVH, D, dist, ch_k)
+        v = _rows(rng, int(n), KVH, D, dist, ch_v)
         t = np.arange(int(n))
         blk, off = bt[b, t // block_size], t % block_size
         kc[blk, :, :, off, :] = k.reshape(int(n), KVH, D // 8, 8)

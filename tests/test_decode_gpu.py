@@ -102,13 +102,13 @@ def test_int8_long_contexts(variant, mode, clen, num_heads, num_kv_heads):
 @pytest.mark.parametrize("splitk", [False, True])
 def test_gqa_shapes(num_heads, num_kv_heads, kind, splitk):
     lens = [700, 33, 1, 1500]
-    c = fp16_case(2, 4, num_heads, num_kv_heads, lens, dist="lognormal_outlier")
+    c = ragged_case(2, num_heads, num_kv_heads, lens, dist="lognormal_outlier")
     if kind == "fp16":
         out = _run_fp16("splitk" if splitk else "warp", c)
         ref = oracle_out(c["q"], c["k_cache"], c["v_cache"], c["block_table"],
                          c["context_lens"])
     else:
-        qc = int8_case(c, "per_token")
+        qc = ragged_int8(c)
         out = _run_int8("splitk_int8" if splitk else "warp_int8", c, qc)
         ref = _int8_oracle(c, qc)
     assert_close(out, ref)
