@@ -1,6 +1,7 @@
 """Shared helpers for the parity tests: seeded inputs (oracle/gen.py), the numpy oracle, and
 torch tensors on the GPU built from the same host arrays."""
 
+import collections
 import math
 
 import numpy as np
@@ -21,15 +22,30 @@ def make_lens(clen, num_seqs):
     return [max(1, clen - 5 * b) for b in range(num_seqs)]
 
 
+_CASES = collections.OrderedDict()  # recent fp16_case results (the variant names share cases)
+_CASES_MAX = 24
+
+
 def fp16_case(seed, num_seqs, num_heads, num_kv_heads, lens, block_size=BLOCK_SIZE,
               dist="normal", extra_blocks=1, max_blocks=None):
-    need = sum((c + block_size - 1) // block_size for c in lens)
-    c = gen.decode_case(seed, num_seqs, num_heads, num_kv_heads, lens, block_size=block_size,
-                        num_blocks=need + extra_blocks, dist=dist, max_blocks=max_blocks)
-    kc, vc = pa_oracle.scatter_paged_cache(c["k"], c["v"], c["context_lens"], c["block_table"],
-                                           c["num_blocks"], block_size)
-    c["k_cache"], c["v_cache"] = kc, vc
-    return c
+    """gen.decode_case plus its fp16 paged cache. Recent cases are kept and handed out as
+    fresh copies, so callers may modify what they get."""
+    key = (seed, num_seqs, num_heads, num_kv_heads, tuple(int(n) for n in lens), block_size,
+           dist, extra_blocks, max_blocks)
+    c = _CASES.get(key)
+    if c is None:
+        need = sum((int(n) + block_size - 1) // block_size for n in lens)
+        c = gen.decode_case(seed, num_seqs, num_heads, num_kv_heads, lens,
+                            block_size=block_size, num_blocks=need + extra_blocks, dist=dist,
+                            max_blocks=max_blocks)
+        c["k_cache"], c["v_cache"] = pa_oracle.scatter_paged_cache(
+            c["k"], c["v"], c["context_lens"], c["block_table"], c["num_blocks"], block_size)
+        _CASES[key] = c
+        if len(_CASES) > _CASES_MAX:
+            _CASES.popitem(last=False)
+    else:
+        _CASES.move_to_end(key)
+    return {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in c.items()}
 
 
 def int8_case(c, mode, block_size=BLOCK_SIZE):
