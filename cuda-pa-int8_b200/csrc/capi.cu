@@ -22,13 +22,18 @@ namespace {
 
 thread_local std::string g_err;
 
-int fail(int code, const char* fmt, ...) {
+int vfail(int code, const char* fmt, va_list ap) {
   char buf[512];
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  g_err = buf;
+  return code;
+}
+
+int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
-  vsnprintf(buf, sizeof(buf), fmt, ap);
+  vfail(code, fmt, ap);
   va_end(ap);
-  g_err = buf;
   return code;
 }
 
@@ -357,6 +362,28 @@ int check_in_dtype(int dt) {
 }
 
 int elem_size(int dt) { return dt == PA_DTYPE_F32 ? 4 : (dt == PA_DTYPE_I8 ? 1 : 2); }
+
+// Checks shared by the token-granular cache writes, in the order they are reported. scales:
+// whether k_scales / v_scales are required; cache_align: byte alignment of the kernel's cache
+// stores (4 for one-byte caches, 8 for fp16).
+int check_row_write(int in_dtype, const void* k, const void* v, int64_t token_stride,
+                    const int32_t* slot_mapping, int num_tokens, int num_kv_heads, int head_dim,
+                    const void* k_cache, const void* v_cache, bool scales, const float* k_scales,
+                    const float* v_scales, int num_blocks, int block_size, size_t cache_align) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || num_blocks <= 0 || block_size <= 0)
+    return fail(PA_ERR_INVALID_ARG, "invalid sizes");
+  if (head_dim != 128) return fail(PA_ERR_UNSUPPORTED, "head_dim %d unsupported", head_dim);
+  if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_cache == nullptr ||
+      v_cache == nullptr || (scales && (k_scales == nullptr || v_scales == nullptr)))
+    return fail(PA_ERR_INVALID_ARG, "null pointer argument");
+  if (token_stride < (int64_t)num_kv_heads * head_dim)
+    return fail(PA_ERR_INVALID_ARG, "token_stride smaller than num_kv_heads*head_dim");
+  const size_t es = (size_t)elem_size(in_dtype);
+  if (!aligned(k, es * 4) || !aligned(v, es * 4) || token_stride % 4 != 0 ||
+      !aligned(k_cache, cache_align) || !aligned(v_cache, cache_align))
+    return fail(PA_ERR_INVALID_ARG, "misaligned input or cache pointer");
+  return PA_OK;
+}
 // Cache kind of the decode kernels: 0 fp16, 1 int8, 2 fp8 e4m3 (-1: not a cache dtype).
 int kv_kind(int kv_dtype) {
   return kv_dtype == PA_DTYPE_F16 ? 0
@@ -368,12 +395,10 @@ int kv_kind(int kv_dtype) {
 
 namespace pa {
 int fail_status(int code, const char* fmt, ...) {
-  char buf[512];
   va_list ap;
   va_start(ap, fmt);
-  vsnprintf(buf, sizeof(buf), fmt, ap);
+  vfail(code, fmt, ap);
   va_end(ap);
-  g_err = buf;
   return code;
 }
 }  // namespace pa
@@ -390,8 +415,10 @@ const char* pa_status_string(int status) {
   if (status & PA_ERR_UNSUPPORTED) return "unsupported shape or dtype";
   if (status & PA_ERR_CUDA) return "CUDA error";
   if (status & PA_ERR_WORKSPACE) return "workspace too small";
-  if (status & PA_ERR_EMPTY_CONTEXT) return "context_lens must be >= 1 (empty sequences unsupported)";
-  if (status & PA_ERR_CONTEXT_RANGE) return "context length exceeds max_blocks_per_seq * block_size";
+  if (status & PA_ERR_EMPTY_CONTEXT)
+    return "context_lens must be >= 1 (empty sequences unsupported)";
+  if (status & PA_ERR_CONTEXT_RANGE)
+    return "context length exceeds max_blocks_per_seq * block_size";
   if (status & PA_ERR_BLOCK_ID) return "block_table entry outside [0, num_blocks)";
   if (status & PA_ERR_TIMEOUT) return "device wait timed out";
   if (status & PA_ERR_SLOT) return "slot_mapping entry outside the cache";
@@ -494,7 +521,8 @@ int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v
                     int kv_dtype, int splitk, float scale, void* workspace,
                     size_t workspace_bytes, void* stream) {
   if (kv_kind(kv_dtype) < 0)
-    return fail(PA_ERR_UNSUPPORTED, "kv_dtype must be PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3");
+    return fail(PA_ERR_UNSUPPORTED,
+                "kv_dtype must be PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3");
   int rc = check_common(num_seqs, num_heads, num_kv_heads, head_dim, num_blocks, block_size,
                         max_blocks_per_seq);
   if (rc != PA_OK) return rc;
@@ -624,19 +652,11 @@ int pa_quantize_into_cache(const void* k, const void* v, int in_dtype, int64_t t
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (num_tokens == 0) return PA_OK;
-  if (num_tokens < 0 || num_kv_heads <= 0 || num_blocks <= 0 || block_size <= 0)
-    return fail(PA_ERR_INVALID_ARG, "invalid sizes");
-  if (head_dim != 128) return fail(PA_ERR_UNSUPPORTED, "head_dim %d unsupported", head_dim);
-  if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_cache == nullptr ||
-      v_cache == nullptr || k_scales == nullptr || v_scales == nullptr)
-    return fail(PA_ERR_INVALID_ARG, "null pointer argument");
-  if (token_stride < (int64_t)num_kv_heads * head_dim)
-    return fail(PA_ERR_INVALID_ARG, "token_stride smaller than num_kv_heads*head_dim");
-  const size_t es = (size_t)elem_size(in_dtype);
-  if (!aligned(k, es * 4) || !aligned(v, es * 4) || ((size_t)token_stride * es) % (es * 4) != 0 ||
-      !aligned(k_cache, 4) || !aligned(v_cache, 4))
-    return fail(PA_ERR_INVALID_ARG, "misaligned input or cache pointer");
-  cudaError_t e = pa::launch_write_rows(in_dtype, true, head_dim, k, v, token_stride,
+  rc = check_row_write(in_dtype, k, v, token_stride, slot_mapping, num_tokens, num_kv_heads,
+                       head_dim, k_cache, v_cache, true, k_scales, v_scales, num_blocks,
+                       block_size, 4);
+  if (rc != PA_OK) return rc;
+  cudaError_t e = pa::launch_write_rows(in_dtype, pa::kRowsI8, head_dim, k, v, token_stride,
                                         slot_mapping, num_tokens, num_kv_heads, k_cache, v_cache,
                                         k_scales, v_scales, num_blocks, block_size,
                                         k_fixed_scale, v_fixed_scale, status,
@@ -653,22 +673,14 @@ int pa_quantize_into_cache_fp8(const void* k, const void* v, int in_dtype, int64
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (num_tokens == 0) return PA_OK;
-  if (num_tokens < 0 || num_kv_heads <= 0 || num_blocks <= 0 || block_size <= 0)
-    return fail(PA_ERR_INVALID_ARG, "invalid sizes");
-  if (head_dim != 128) return fail(PA_ERR_UNSUPPORTED, "head_dim %d unsupported", head_dim);
-  if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_cache == nullptr ||
-      v_cache == nullptr || k_scales == nullptr || v_scales == nullptr)
-    return fail(PA_ERR_INVALID_ARG, "null pointer argument");
-  if (token_stride < (int64_t)num_kv_heads * head_dim)
-    return fail(PA_ERR_INVALID_ARG, "token_stride smaller than num_kv_heads*head_dim");
-  const size_t es = (size_t)elem_size(in_dtype);
-  if (!aligned(k, es * 4) || !aligned(v, es * 4) || ((size_t)token_stride * es) % (es * 4) != 0 ||
-      !aligned(k_cache, 4) || !aligned(v_cache, 4))
-    return fail(PA_ERR_INVALID_ARG, "misaligned input or cache pointer");
-  cudaError_t e = pa::launch_write_rows(in_dtype, 2, head_dim, k, v, token_stride, slot_mapping,
-                                        num_tokens, num_kv_heads, k_cache, v_cache, k_scales,
-                                        v_scales, num_blocks, block_size, nullptr, nullptr,
-                                        status, static_cast<cudaStream_t>(stream));
+  rc = check_row_write(in_dtype, k, v, token_stride, slot_mapping, num_tokens, num_kv_heads,
+                       head_dim, k_cache, v_cache, true, k_scales, v_scales, num_blocks,
+                       block_size, 4);
+  if (rc != PA_OK) return rc;
+  cudaError_t e = pa::launch_write_rows(in_dtype, pa::kRowsFP8, head_dim, k, v, token_stride,
+                                        slot_mapping, num_tokens, num_kv_heads, k_cache, v_cache,
+                                        k_scales, v_scales, num_blocks, block_size, nullptr,
+                                        nullptr, status, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "fp8 quantize launch");
   return PA_OK;
 }
@@ -680,19 +692,11 @@ int pa_write_into_cache_f16(const void* k, const void* v, int in_dtype, int64_t 
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (num_tokens == 0) return PA_OK;
-  if (num_tokens < 0 || num_kv_heads <= 0 || num_blocks <= 0 || block_size <= 0)
-    return fail(PA_ERR_INVALID_ARG, "invalid sizes");
-  if (head_dim != 128) return fail(PA_ERR_UNSUPPORTED, "head_dim %d unsupported", head_dim);
-  if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_cache == nullptr ||
-      v_cache == nullptr)
-    return fail(PA_ERR_INVALID_ARG, "null pointer argument");
-  if (token_stride < (int64_t)num_kv_heads * head_dim)
-    return fail(PA_ERR_INVALID_ARG, "token_stride smaller than num_kv_heads*head_dim");
-  const size_t es = (size_t)elem_size(in_dtype);
-  if (!aligned(k, es * 4) || !aligned(v, es * 4) || ((size_t)token_stride * es) % (es * 4) != 0 ||
-      !aligned(k_cache, 8) || !aligned(v_cache, 8))
-    return fail(PA_ERR_INVALID_ARG, "misaligned input or cache pointer");
-  cudaError_t e = pa::launch_write_rows(in_dtype, false, head_dim, k, v, token_stride,
+  rc = check_row_write(in_dtype, k, v, token_stride, slot_mapping, num_tokens, num_kv_heads,
+                       head_dim, k_cache, v_cache, false, nullptr, nullptr, num_blocks,
+                       block_size, 8);
+  if (rc != PA_OK) return rc;
+  cudaError_t e = pa::launch_write_rows(in_dtype, pa::kRowsF16, head_dim, k, v, token_stride,
                                         slot_mapping, num_tokens, num_kv_heads, k_cache, v_cache,
                                         nullptr, nullptr, num_blocks, block_size, nullptr,
                                         nullptr, status, static_cast<cudaStream_t>(stream));
@@ -722,7 +726,8 @@ int pa_prefill_into_cache(const void* k, const void* v, int in_dtype, int num_se
     return fail(PA_ERR_INVALID_ARG, "block_size must be a multiple of 16 up to 128");
   const bool i8 = cache_dtype == PA_DTYPE_I8;
   if (k == nullptr || v == nullptr || block_table == nullptr || context_lens == nullptr ||
-      k_cache == nullptr || v_cache == nullptr || (i8 && (k_scales == nullptr || v_scales == nullptr)))
+      k_cache == nullptr || v_cache == nullptr ||
+      (i8 && (k_scales == nullptr || v_scales == nullptr)))
     return fail(PA_ERR_INVALID_ARG, "null pointer argument");
   const size_t es = (size_t)elem_size(in_dtype);
   if (!aligned(k, es * 4) || !aligned(v, es * 4) || !aligned(k_cache, 16) || !aligned(v_cache, 16))

@@ -4,8 +4,9 @@
 // whose host framework owns every device allocation and hands out only tensor pointers
 // (the plugin has no allocator of its own to call), and latency-critical serving loops that
 // must never enter an allocator (it can synchronise the device or fail when memory is
-// fragmented, mid-step). This entry point serves them: its scratch (status word, arrival counters, partial slots) lives
-// in one statically sized device array that belongs to this file.
+// fragmented, mid-step). This entry point serves them: its scratch (status word, arrival
+// counters, partial slots) lives in one statically sized device array that belongs to this
+// file.
 //
 // The array holds kNoAllocScratchBytes (12 MiB) on every GPU whose context loads this code,
 // until the process exits. Every call on a device shares it and it keeps the last call's

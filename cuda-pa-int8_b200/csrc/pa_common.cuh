@@ -120,7 +120,8 @@ __device__ __forceinline__ void prefetch_l2_share(const void* base, size_t bytes
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA: 1-D bulk copies and tiled tensor copies into this CTA's shared memory, completing on an mbarrier
+// TMA: 1-D bulk copies and tiled tensor copies into this CTA's shared memory, completing on an
+// mbarrier
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {

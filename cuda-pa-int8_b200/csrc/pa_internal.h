@@ -63,7 +63,12 @@ cudaError_t launch_decode(int kv_i8, int gt, const DecodeArgs& a, const CUtensor
                           int grid, cudaStream_t stream);
 cudaError_t launch_reduce(int gt, const ReduceArgs& a, int max_pieces, cudaStream_t stream);
 int decode_warps_per_cta(int kv_i8, int gt);
-// kind: 0 fp16 copy, 1 int8 (per-token or fixed scale), 2 fp8 e4m3 (per-token scale).
+// Token-granular cache writes; kind selects the cache type.
+enum RowKind {
+  kRowsF16 = 0,  // fp16 copy
+  kRowsI8 = 1,   // int8, per-token or fixed scale
+  kRowsFP8 = 2,  // fp8 e4m3, per-token scale
+};
 cudaError_t launch_write_rows(int in_dtype, int kind, int D, const void* k, const void* v,
                               long long token_stride, const int* slots, int N, int KVH,
                               void* kc, void* vc, float* ks, float* vs, int NB, int bs,

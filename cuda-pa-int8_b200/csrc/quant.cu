@@ -358,11 +358,11 @@ cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long lo
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
   if (D != 128) return cudaErrorInvalidValue;
-  if (kind == 2) {
+  if (kind == kRowsFP8) {
     write_rows_fp8_kernel<T, 128><<<grid, 256, 0, st>>>(
         kk, vv, ts, slots, N, KVH, static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), ks, vs,
         NB, bs, status);
-  } else if (kind == 1) {
+  } else if (kind == kRowsI8) {
     write_rows_kernel<T, true, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc, ks,
                                                           vs, NB, bs, kf, vf, status);
   } else {
@@ -442,7 +442,8 @@ cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float*
   const int grid = num_sms * 4;
   switch (in_dtype) {
     case PA_DTYPE_F16:
-      if (n > 0) absmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), n, scratch);
+      if (n > 0)
+        absmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), n, scratch);
       scale_finalize_kernel<__half><<<1, 1, 0, st>>>(scratch, scale_out, semantics);
       break;
     case PA_DTYPE_BF16:
@@ -452,7 +453,8 @@ cudaError_t launch_absmax_scale(int in_dtype, const void* x, long long n, float*
       scale_finalize_kernel<__nv_bfloat16><<<1, 1, 0, st>>>(scratch, scale_out, semantics);
       break;
     case PA_DTYPE_F32:
-      if (n > 0) absmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), n, scratch);
+      if (n > 0)
+        absmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), n, scratch);
       scale_finalize_kernel<float><<<1, 1, 0, st>>>(scratch, scale_out, semantics);
       break;
     default:

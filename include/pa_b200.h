@@ -69,8 +69,8 @@ const char* pa_status_string(int status);
 
 /* ------------------------------------------------------------------------------------
  * Decode workspace size for one call shape on the current device (0 for an unsupported
- * shape). kv_dtype is PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3; splitk selects the split-K partition/reduce pair (nonzero) or the
- * single-pass op (zero).
+ * shape). kv_dtype is PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3; splitk selects the
+ * split-K partition/reduce pair (nonzero) or the single-pass op (zero).
  * ---------------------------------------------------------------------------------- */
 size_t pa_decode_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, int head_dim,
                                  int max_blocks_per_seq, int block_size, int kv_dtype,
@@ -148,12 +148,13 @@ int pa_decode_f16_noalloc(void* out, const void* q, const void* k_cache, const v
 
 /* Decode with bf16 activations: q and out are bf16 [num_seqs, num_heads, head_dim]; the cache
  * is fp16 (kv_dtype PA_DTYPE_F16), per-token int8 (PA_DTYPE_I8) or per-token fp8 e4m3
- * (PA_DTYPE_FP8E4M3), the last two with k_scales/v_scales; splitk selects the split-K pair. q is converted to fp16 on the device (exact for magnitudes
- * in the fp16 normal range; larger values saturate and set PA_ERR_Q_RANGE in the status word),
- * the fp16 decode runs, and its output is rounded once to bf16. The workspace holds the decode
- * workspace followed by the fp16 copies: size it with pa_decode_bf16q_workspace_bytes. This is
- * the BF16-q support the reference lists as future work (report/benchmark_report.md:196-197);
- * the reference's own ops take fp16 q only. */
+ * (PA_DTYPE_FP8E4M3), the last two with k_scales/v_scales; splitk selects the split-K pair.
+ * q is converted to fp16 on the device (exact for magnitudes in the fp16 normal range; larger
+ * values saturate and set PA_ERR_Q_RANGE in the status word), the fp16 decode runs, and its
+ * output is rounded once to bf16. The workspace holds the decode workspace followed by the
+ * fp16 copies: size it with pa_decode_bf16q_workspace_bytes. This is the BF16-q support the
+ * reference lists as future work (report/benchmark_report.md:196-197); the reference's own
+ * ops take fp16 q only. */
 size_t pa_decode_bf16q_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads,
                                        int head_dim, int max_blocks_per_seq, int block_size,
                                        int kv_dtype, int splitk);
