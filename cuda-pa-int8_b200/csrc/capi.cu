@@ -16,6 +16,8 @@
 #include <mutex>
 #include <string>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "pa_internal.h"
 
 namespace {
@@ -42,6 +44,16 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// An NVTX range named after the entry point, around its host work and launches, so profiler
+// timelines (nsys, ncu's NVTX filters) show which library call issued which kernels. Without
+// an attached tool the NVTX calls return immediately.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // ---- device properties ------------------------------------------------------------------
 int num_sms_current(int* dev_out) {
@@ -460,6 +472,7 @@ int pa_decode_f16(void* out, const void* q, const void* k_cache, const void* v_c
                   int num_heads, int num_kv_heads, int head_dim, int num_blocks, int block_size,
                   int max_blocks_per_seq, float scale, void* workspace, size_t workspace_bytes,
                   void* stream) {
+  const NvtxRange nvtx_range("pa_decode_f16");
   return decode_impl(pa::kModeStream, 0, out, nullptr, q, k_cache, v_cache, nullptr, nullptr,
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
@@ -471,6 +484,7 @@ int pa_decode_i8(void* out, const void* q, const void* k_cache, const void* v_ca
                  const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                  float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  const NvtxRange nvtx_range("pa_decode_i8");
   return decode_impl(pa::kModeStream, 1, out, nullptr, q, k_cache, v_cache, k_scales, v_scales,
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
@@ -482,6 +496,7 @@ int pa_splitk_f16(void* out, const void* q, const void* k_cache, const void* v_c
                   int num_heads, int num_kv_heads, int head_dim, int num_blocks, int block_size,
                   int max_blocks_per_seq, float scale, void* workspace, size_t workspace_bytes,
                   void* stream) {
+  const NvtxRange nvtx_range("pa_splitk_f16");
   return decode_impl(pa::kModeSplit, 0, out, nullptr, q, k_cache, v_cache, nullptr, nullptr,
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
@@ -493,6 +508,7 @@ int pa_splitk_i8(void* out, const void* q, const void* k_cache, const void* v_ca
                  const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
                  int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                  float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  const NvtxRange nvtx_range("pa_splitk_i8");
   return decode_impl(pa::kModeSplit, 1, out, nullptr, q, k_cache, v_cache, k_scales, v_scales,
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
@@ -520,6 +536,7 @@ int pa_decode_bf16q(void* out, const void* q, const void* k_cache, const void* v
                     int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                     int kv_dtype, int splitk, float scale, void* workspace,
                     size_t workspace_bytes, void* stream) {
+  const NvtxRange nvtx_range("pa_decode_bf16q");
   if (kv_kind(kv_dtype) < 0)
     return fail(PA_ERR_UNSUPPORTED,
                 "kv_dtype must be PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3");
@@ -573,6 +590,7 @@ int pa_decode_fp8(void* out, const void* q, const void* k_cache, const void* v_c
                   const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
                   int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                   float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  const NvtxRange nvtx_range("pa_decode_fp8");
   return decode_impl(pa::kModeStream, 2, out, nullptr, q, k_cache, v_cache, k_scales, v_scales,
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
@@ -584,6 +602,7 @@ int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_c
                   const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
                   int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                   float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  const NvtxRange nvtx_range("pa_splitk_fp8");
   return decode_impl(pa::kModeSplit, 2, out, nullptr, q, k_cache, v_cache, k_scales, v_scales,
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
@@ -603,6 +622,7 @@ int pa_decode_partial(int kv_dtype, float* partials, const void* q, const void* 
                       int num_heads, int num_kv_heads, int head_dim, int num_blocks,
                       int block_size, int max_blocks_per_seq, float scale, void* workspace,
                       size_t workspace_bytes, void* stream) {
+  const NvtxRange nvtx_range("pa_decode_partial");
   if (kv_kind(kv_dtype) < 0)
     return fail(PA_ERR_UNSUPPORTED, "kv dtype must be fp16, int8 or fp8 e4m3");
   return decode_impl(pa::kModePartial, kv_kind(kv_dtype), nullptr, partials, q,
@@ -614,6 +634,7 @@ int pa_decode_partial(int kv_dtype, float* partials, const void* q, const void* 
 int pa_merge_partials(void* out, const float* partials, int num_parts, int num_seqs,
                       int num_heads, int num_kv_heads, int head_dim, int* status,
                       void* stream) {
+  const NvtxRange nvtx_range("pa_merge_partials");
   if (num_seqs == 0) return PA_OK;
   if (out == nullptr || partials == nullptr || num_parts <= 0 || num_seqs < 0 ||
       num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
@@ -649,6 +670,7 @@ int pa_quantize_into_cache(const void* k, const void* v, int in_dtype, int64_t t
                            float* v_scales, int num_blocks, int block_size,
                            const float* k_fixed_scale, const float* v_fixed_scale, int* status,
                            void* stream) {
+  const NvtxRange nvtx_range("pa_quantize_into_cache");
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (num_tokens == 0) return PA_OK;
@@ -670,6 +692,7 @@ int pa_quantize_into_cache_fp8(const void* k, const void* v, int in_dtype, int64
                                int head_dim, void* k_cache, void* v_cache, float* k_scales,
                                float* v_scales, int num_blocks, int block_size, int* status,
                                void* stream) {
+  const NvtxRange nvtx_range("pa_quantize_into_cache_fp8");
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (num_tokens == 0) return PA_OK;
@@ -689,6 +712,7 @@ int pa_write_into_cache_f16(const void* k, const void* v, int in_dtype, int64_t 
                             const int32_t* slot_mapping, int num_tokens, int num_kv_heads,
                             int head_dim, void* k_cache, void* v_cache, int num_blocks,
                             int block_size, int* status, void* stream) {
+  const NvtxRange nvtx_range("pa_write_into_cache_f16");
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (num_tokens == 0) return PA_OK;
@@ -711,6 +735,7 @@ int pa_prefill_into_cache(const void* k, const void* v, int in_dtype, int num_se
                           float* k_scales, float* v_scales, int num_blocks, int block_size,
                           const float* k_fixed_scale, const float* v_fixed_scale, int* status,
                           void* stream) {
+  const NvtxRange nvtx_range("pa_prefill_into_cache");
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (cache_dtype != PA_DTYPE_I8 && cache_dtype != PA_DTYPE_F16)
@@ -743,6 +768,7 @@ int pa_prefill_into_cache(const void* k, const void* v, int in_dtype, int num_se
 
 int pa_absmax_scale(const void* x, int in_dtype, int64_t n, float* scale_out, int semantics,
                     void* scratch, void* stream) {
+  const NvtxRange nvtx_range("pa_absmax_scale");
   int rc = check_in_dtype(in_dtype);
   if (rc != PA_OK) return rc;
   if (scale_out == nullptr || scratch == nullptr || (n > 0 && x == nullptr) || n < 0)
