@@ -11,6 +11,7 @@ Other configs (parity cases and DESIGN.md numbers): 3 INT8 per-token decode + on
 quantize-write per sequence (B64, ctx 8192, 12/2); 4 long-context split-K INT8 sharded by
 kv-head (B8, ctx U[65536,131072], 64/8); 5 ragged INT8 serving batch + one-token write per
 sequence, sequences LPT-sharded across ranks (B256, 28/4, ctx lognormal median 2048 sigma 1).
+Configs 4 and 5 divide one fixed workload among the ranks (strong scaling).
 Inputs are synthetic (seeded), far larger than L2 (126 MB) for configs 2-5 except where
 noted in the JSON; timing is CUDA events on the launching stream, max over ranks.
 --impl reference times the reference algorithm's CPU implementation (the oracle port) on a
@@ -33,6 +34,12 @@ HEAD_DIM = 128
 BLOCK = 16
 METRIC = "paged-decode achieved HBM GB/s (% of B200 peak) and seqs/sec at 1/2/4/8 GPUs"
 NOMINAL_GBS = 8000.0
+
+
+def scaling_of(cfg):
+    """Configs 4 and 5 split one fixed workload across the ranks (by kv head, by sequence):
+    strong scaling. The others give every rank its own batch: weak scaling."""
+    return "strong" if cfg in (4, 5) else "weak"
 
 
 def parse():
@@ -352,8 +359,8 @@ def main():
         base = cpu_baseline(args.config, steps=args.steps, warmup=args.warmup)
         line = {"metric": METRIC, "value": base["value"], "unit": "GB/s", "impl": "reference",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f32", "data": "synthetic",
+                "higher_is_better": True, "scaling": scaling_of(args.config),
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": config_desc(args.config, None, args.splitk),
                 "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -433,6 +440,8 @@ def main():
         total_bytes, total_seqs = float(tot[0]), float(tot[1])
     else:
         total_bytes, total_seqs = float(w.step_bytes), float(w.B)
+    if args.config == 4:
+        total_seqs = float(w.B)  # every rank decodes all sequences, for its share of kv heads
     del g_step, g_dec
     from pa_b200 import ops
     status = ops.read_status(device)
@@ -497,7 +506,8 @@ def main():
     kernel_gbs = float(w.decode_bytes) / (dec_ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": scaling_of(args.config),
         "vs_baseline": None, "dtype": "fp8_e4m3" if w.fp8 else ("int8" if w.int8 else "f16"),
         "data": "synthetic",
         "config": config_desc(args.config, w, args.splitk),
@@ -516,6 +526,7 @@ def main():
         "device_status": status,
         "clocks": clocks,
     }
+    line["config"]["global_batch"] = int(total_seqs)
     if e2e:
         line["e2e"] = e2e
     if rank == 0 and not args.no_cpu_baseline and world == 1:
