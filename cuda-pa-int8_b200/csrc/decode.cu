@@ -75,13 +75,13 @@ struct Tile {
 
 // ---------------------------------------------------------------------------------------
 // Warp-level log-sum-exp merge for segments with few pieces (np <= 32): lane k reads piece
-// k's maxima and denominators; the O rows are then accumulated two pieces per step, each
+// k's maxima and denominators; the O rows are then accumulated P pieces per step, each
 // lane owning head_dim rows [lane*D/32, (lane+1)*D/32). Several of these run in parallel,
 // one per warp.
 // ---------------------------------------------------------------------------------------
 constexpr int kWarpMergeMax = 32;
 
-template <int D, int GT, typename PieceFn>
+template <int D, int GT, int P, typename PieceFn>
 __device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, int hcnt,
                                              __half* out_rows, float* out_slot, int* status) {
   constexpr int DPL = D / 32;
@@ -102,52 +102,48 @@ __device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, in
       lk[4 * h4 + 0] = l4.x; lk[4 * h4 + 1] = l4.y; lk[4 * h4 + 2] = l4.z; lk[4 * h4 + 3] = l4.w;
     }
   }
-  // The first step's O rows do not depend on the weights: their loads overlap the maxima's.
-  float4 v0[Q], v1[Q];
-  {
-    const float4* r0 = reinterpret_cast<const float4*>(piece(0) + lane * DPL * GT);
-    const float4* r1 = reinterpret_cast<const float4*>(piece(np > 1 ? 1 : 0) + lane * DPL * GT);
+  // O rows of P pieces per step (a piece past np reloads piece k and gets weight 0). The
+  // first step's loads do not depend on the weights, so they overlap the maxima's.
+  float4 v[P][Q];
+  auto load_step = [&](int k) {
 #pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      v0[q] = __ldcg(r0 + q);
-      v1[q] = __ldcg(r1 + q);
+    for (int p = 0; p < P; ++p) {
+      const int kk = (k + p < np) ? k + p : k;
+      const float4* r = reinterpret_cast<const float4*>(piece(kk) + lane * DPL * GT);
+#pragma unroll
+      for (int q = 0; q < Q; ++q) v[p][q] = __ldcg(r + q);
     }
-  }
+  };
+  load_step(0);
   float wk[GT], L[GT], M[GT];
 #pragma unroll
   for (int h = 0; h < GT; ++h) {
     M[h] = warp_max(mk[h]);
     wk[h] = (M[h] == neg_inf() || lane >= np) ? 0.f : ex2(mk[h] - M[h]);
-    float v = wk[h] * lk[h];
+    float s = wk[h] * lk[h];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    L[h] = v;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    L[h] = s;
   }
   float acc[DPL * GT];
 #pragma unroll
   for (int i = 0; i < DPL * GT; ++i) acc[i] = 0.f;
-  for (int k = 0; k < np; k += 2) {
-    const bool two = (k + 1) < np;
-    if (k > 0) {
-      const float4* r0 = reinterpret_cast<const float4*>(piece(k) + lane * DPL * GT);
-      const float4* r1 =
-          reinterpret_cast<const float4*>(piece(two ? k + 1 : k) + lane * DPL * GT);
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        v0[q] = __ldcg(r0 + q);
-        v1[q] = __ldcg(r1 + q);
-      }
-    }
+  for (int k = 0; k < np; k += P) {
+    if (k > 0) load_step(k);
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
       const int h = (4 * q) % GT;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float w0 = __shfl_sync(0xffffffffu, wk[h + e], k);
-        const float w1 = two ? __shfl_sync(0xffffffffu, wk[h + e], k + 1) : 0.f;
-        const float a0 = e == 0 ? v0[q].x : e == 1 ? v0[q].y : e == 2 ? v0[q].z : v0[q].w;
-        const float a1 = e == 0 ? v1[q].x : e == 1 ? v1[q].y : e == 2 ? v1[q].z : v1[q].w;
-        acc[4 * q + e] += w0 * a0 + w1 * a1;
+        float s = 0.f;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          const float w = (k + p < np) ? __shfl_sync(0xffffffffu, wk[h + e], k + p) : 0.f;
+          const float x = e == 0 ? v[p][q].x : e == 1 ? v[p][q].y : e == 2 ? v[p][q].z
+                                                                         : v[p][q].w;
+          s += w * x;
+        }
+        acc[4 * q + e] += s;
       }
     }
   }
@@ -1332,6 +1328,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // piece and never merge in a single warp.
   int n_merges = 0;
   for (int w = 0; w < WARPS; ++w) n_merges += s_npend[w];
+  // Pieces per step of a one-warp merge: four where the launch leaves 255 registers a thread
+  // (8 warps), two under the 168 of 12-warp launches.
+  constexpr int kWarpStep = (WARPS <= 8) ? 4 : 2;
   const int kWarpMerge =
       (GT != 8) ? 0 : (n_merges * 4 >= WARPS ? kWarpMergeMax : 4);
   int idx = 0;
@@ -1346,11 +1345,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
       };
       if (a.mode == kModeStream) {
-        warp_combine<D, GT>(piece, np, lane, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
-                            nullptr, a.status);
+        warp_combine<D, GT, kWarpStep>(piece, np, lane, hcnt,
+                                       a.out + ((size_t)b * a.H + hbase) * D, nullptr, a.status);
       } else {
-        warp_combine<D, GT>(piece, np, lane, hcnt, nullptr, a.part_out + (size_t)segid * SLOT,
-                            a.status);
+        warp_combine<D, GT, kWarpStep>(piece, np, lane, hcnt, nullptr,
+                                       a.part_out + (size_t)segid * SLOT, a.status);
       }
       if (lane == 0) a.counters[segid] = 0;
     }
