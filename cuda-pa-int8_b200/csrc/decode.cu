@@ -836,7 +836,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     return pk;
   };
   int cur = batch_info(0);
-  int nxt = batch_info(32);
+  int nxt = 0;  // block ids of pages 32..63: read once the first copies are on their way
 
   auto issue = [&](int j, int s) {
     if (j > 0 && (j & 31) == 0) {
@@ -874,10 +874,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
+  static_assert(DEPTH < 32, "the prologue copies must come from the first batch of block ids");
   const int npro = n < DEPTH ? n : DEPTH;
   __syncwarp();
   for (int j = 0; j < npro; ++j) issue(j, j);
   int issued = npro;
+  nxt = batch_info(32);
   convert_q();
 
   // Shared-memory offsets of the K cells this lane reads (chunk of load si, token of n-tile
