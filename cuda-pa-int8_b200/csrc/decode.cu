@@ -79,7 +79,9 @@ struct Tile {
 // lane owning head_dim rows [lane*D/32, (lane+1)*D/32). Several of these run in parallel,
 // one per warp.
 // ---------------------------------------------------------------------------------------
-constexpr int kWarpMergeMax = 32;
+// Largest merge a single warp takes when its CTA owes many merges; larger ones go to the
+// four-warp groups, whose merges need fewer dependent round trips.
+constexpr int kWarpMergeMax = 8;
 
 template <int D, int GT, int P, typename PieceFn>
 __device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, int hcnt,
