@@ -75,13 +75,15 @@ struct Tile {
 
 // ---------------------------------------------------------------------------------------
 // Warp-level log-sum-exp merge for segments with few pieces (np <= 32): lane k reads piece
-// k's maxima and denominators; the O rows are then accumulated two pieces per step, each
+// k's maxima and denominators; the O rows are then accumulated P pieces per step, each
 // lane owning head_dim rows [lane*D/32, (lane+1)*D/32). Several of these run in parallel,
 // one per warp.
 // ---------------------------------------------------------------------------------------
-constexpr int kWarpMergeMax = 32;
+// Largest merge a single warp takes when its CTA owes many merges; larger ones go to the
+// four-warp groups, whose merges need fewer dependent round trips.
+constexpr int kWarpMergeMax = 8;
 
-template <int D, int GT, typename PieceFn>
+template <int D, int GT, int P, typename PieceFn>
 __device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, int hcnt,
                                              __half* out_rows, float* out_slot, int* status) {
   constexpr int DPL = D / 32;
@@ -102,39 +104,48 @@ __device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, in
       lk[4 * h4 + 0] = l4.x; lk[4 * h4 + 1] = l4.y; lk[4 * h4 + 2] = l4.z; lk[4 * h4 + 3] = l4.w;
     }
   }
+  // O rows of P pieces per step (a piece past np reloads piece k and gets weight 0). The
+  // first step's loads do not depend on the weights, so they overlap the maxima's.
+  float4 v[P][Q];
+  auto load_step = [&](int k) {
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int kk = (k + p < np) ? k + p : k;
+      const float4* r = reinterpret_cast<const float4*>(piece(kk) + lane * DPL * GT);
+#pragma unroll
+      for (int q = 0; q < Q; ++q) v[p][q] = __ldcg(r + q);
+    }
+  };
+  load_step(0);
   float wk[GT], L[GT], M[GT];
 #pragma unroll
   for (int h = 0; h < GT; ++h) {
     M[h] = warp_max(mk[h]);
     wk[h] = (M[h] == neg_inf() || lane >= np) ? 0.f : ex2(mk[h] - M[h]);
-    float v = wk[h] * lk[h];
+    float s = wk[h] * lk[h];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    L[h] = v;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    L[h] = s;
   }
   float acc[DPL * GT];
 #pragma unroll
   for (int i = 0; i < DPL * GT; ++i) acc[i] = 0.f;
-  for (int k = 0; k < np; k += 2) {
-    const bool two = (k + 1) < np;
-    float4 v0[Q], v1[Q];
-    const float4* r0 = reinterpret_cast<const float4*>(piece(k) + lane * DPL * GT);
-    const float4* r1 = reinterpret_cast<const float4*>(piece(two ? k + 1 : k) + lane * DPL * GT);
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      v0[q] = __ldcg(r0 + q);
-      v1[q] = __ldcg(r1 + q);
-    }
+  for (int k = 0; k < np; k += P) {
+    if (k > 0) load_step(k);
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
       const int h = (4 * q) % GT;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float w0 = __shfl_sync(0xffffffffu, wk[h + e], k);
-        const float w1 = two ? __shfl_sync(0xffffffffu, wk[h + e], k + 1) : 0.f;
-        const float a0 = e == 0 ? v0[q].x : e == 1 ? v0[q].y : e == 2 ? v0[q].z : v0[q].w;
-        const float a1 = e == 0 ? v1[q].x : e == 1 ? v1[q].y : e == 2 ? v1[q].z : v1[q].w;
-        acc[4 * q + e] += w0 * a0 + w1 * a1;
+        float s = 0.f;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          const float w = (k + p < np) ? __shfl_sync(0xffffffffu, wk[h + e], k + p) : 0.f;
+          const float x = e == 0 ? v[p][q].x : e == 1 ? v[p][q].y : e == 2 ? v[p][q].z
+                                                                         : v[p][q].w;
+          s += w * x;
+        }
+        acc[4 * q + e] += s;
       }
     }
   }
@@ -343,6 +354,199 @@ __device__ __forceinline__ void coop_combine(PieceFn piece, int np, int hcnt, __
     }
   }
   __syncthreads();
+}
+
+// ---------------------------------------------------------------------------------------
+// Log-sum-exp merge of `np` partial slots by one group of GS threads (GS / 32 whole warps) of
+// the CTA, so that the few merges a CTA owes at the end of the launch run side by side
+// instead of one after another. The group synchronises on its own named barrier `bar_id`.
+// The maxima and denominators of all pieces and the O values of the first U pieces are
+// requested together, and the weights are formed from copies of the maxima in shared
+// memory, so a merge of up to U pieces costs one dependent L2 round trip before the output
+// is written (each further U pieces add one).
+// ---------------------------------------------------------------------------------------
+template <int D, int GT, int GS>
+struct Group {
+  static constexpr int OUT4 = D * GT / 4;  // float4 outputs of one merge
+  static_assert(OUT4 % GS == 0, "outputs must tile the group");
+  static constexpr int OPT = OUT4 / GS;    // outputs per thread
+  static constexpr int U = 16 / OPT;       // pieces per output in flight (16 float4 loads)
+  static constexpr int NWG = GS / 32;
+  // Scratch floats for np pieces: M, L, per-warp partials, then np x GT maxima (later the
+  // weights) and np x GT denominators.
+  __host__ __device__ static constexpr size_t floats(int np) {
+    return 2 * GT + NWG * GT + 2 * (((size_t)np * GT + 3) / 4 * 4);
+  }
+};
+
+// Named barriers 1..3 (barrier 0 is __syncthreads), with immediate ids so that the kernel
+// reserves only the barriers it uses.
+__device__ __forceinline__ void group_sync(int bar_id, int nthreads) {
+  if (bar_id == 1) {
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  } else if (bar_id == 2) {
+    asm volatile("bar.sync 2, %0;" ::"r"(nthreads) : "memory");
+  } else {
+    asm volatile("bar.sync 3, %0;" ::"r"(nthreads) : "memory");
+  }
+}
+
+template <int D, int GT, int GS, typename PieceFn>
+__device__ __forceinline__ void group_combine(PieceFn piece, int np, int hcnt, __half* out_rows,
+                                              float* out_slot, int* status, float* sm,
+                                              int gtid, int bar_id) {
+  using G = Group<D, GT, GS>;
+  constexpr int OPT = G::OPT;
+  constexpr int U = G::U;
+  const int lane = gtid & 31, gw = gtid >> 5;
+  float* sM = sm;
+  float* sL = sm + GT;
+  float* sRed = sm + 2 * GT;
+  float* sW = sRed + G::NWG * GT;
+  float* sLk = sW + ((size_t)np * GT + 3) / 4 * 4;
+
+  // O values of the first U pieces: they do not depend on the weights, so they are requested
+  // before the maxima are known.
+  float4 v[OPT][U];
+#pragma unroll
+  for (int i = 0; i < OPT; ++i) {
+    const int o = gtid + i * GS;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      v[i][u] = (u < np) ? __ldcg(reinterpret_cast<const float4*>(piece(u)) + o)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // Maxima and denominators of every piece, kept in shared memory.
+  float mx[GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) mx[h] = neg_inf();
+  for (int k = gtid; k < np; k += GS) {
+    const float4* mk = reinterpret_cast<const float4*>(piece(k) + D * GT);
+#pragma unroll
+    for (int h4 = 0; h4 < GT / 4; ++h4) {
+      const float4 m4 = __ldcg(mk + h4);
+      const float4 l4 = __ldcg(mk + GT / 4 + h4);
+      reinterpret_cast<float4*>(sW + (size_t)k * GT)[h4] = m4;
+      reinterpret_cast<float4*>(sLk + (size_t)k * GT)[h4] = l4;
+      mx[4 * h4 + 0] = fmaxf(mx[4 * h4 + 0], m4.x);
+      mx[4 * h4 + 1] = fmaxf(mx[4 * h4 + 1], m4.y);
+      mx[4 * h4 + 2] = fmaxf(mx[4 * h4 + 2], m4.z);
+      mx[4 * h4 + 3] = fmaxf(mx[4 * h4 + 3], m4.w);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < GT; ++h) {
+    const float m = warp_max(mx[h]);
+    if (lane == 0) sRed[gw * GT + h] = m;
+  }
+  group_sync(bar_id, GS);
+  if (gtid < GT) {
+    float m = neg_inf();
+    for (int w = 0; w < G::NWG; ++w) m = fmaxf(m, sRed[w * GT + gtid]);
+    sM[gtid] = m;
+  }
+  group_sync(bar_id, GS);
+  // Weights w_k = 2^(m_k - M) replace the maxima in place (each thread rewrites the entries
+  // it stored above); the denominators are summed with them.
+  float ls[GT];
+#pragma unroll
+  for (int h = 0; h < GT; ++h) ls[h] = 0.f;
+  for (int k = gtid; k < np; k += GS) {
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+      const float M = sM[h];
+      const float w = (M == neg_inf()) ? 0.f : ex2(sW[(size_t)k * GT + h] - M);
+      sW[(size_t)k * GT + h] = w;
+      ls[h] += w * sLk[(size_t)k * GT + h];
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < GT; ++h) {
+    float s = ls[h];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) sRed[gw * GT + h] = s;
+  }
+  group_sync(bar_id, GS);
+  if (gtid < GT) {
+    float s = 0.f;
+    for (int w = 0; w < G::NWG; ++w) s += sRed[w * GT + gtid];
+    sL[gtid] = s;
+  }
+  group_sync(bar_id, GS);
+
+  // O = sum_k w_k O_k, one float4 (4 heads of one head_dim row) per output.
+  float4 acc[OPT];
+#pragma unroll
+  for (int i = 0; i < OPT; ++i) {
+    const int o = gtid + i * GS;
+    const int h0 = (o % (GT / 4)) * 4;
+    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (u < np) {
+        const float* w = sW + (size_t)u * GT + h0;
+        a4.x += w[0] * v[i][u].x;
+        a4.y += w[1] * v[i][u].y;
+        a4.z += w[2] * v[i][u].z;
+        a4.w += w[3] * v[i][u].w;
+      }
+    }
+    acc[i] = a4;
+  }
+  for (int k0 = U; k0 < np; k0 += U) {
+#pragma unroll
+    for (int i = 0; i < OPT; ++i) {
+      const int o = gtid + i * GS;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        v[i][u] = (k0 + u < np) ? __ldcg(reinterpret_cast<const float4*>(piece(k0 + u)) + o)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < OPT; ++i) {
+      const int o = gtid + i * GS;
+      const int h0 = (o % (GT / 4)) * 4;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (k0 + u < np) {
+          const float* w = sW + (size_t)(k0 + u) * GT + h0;
+          acc[i].x += w[0] * v[i][u].x;
+          acc[i].y += w[1] * v[i][u].y;
+          acc[i].z += w[2] * v[i][u].z;
+          acc[i].w += w[3] * v[i][u].w;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < OPT; ++i) {
+    const int o = gtid + i * GS;
+    const int d = o / (GT / 4);
+    const int h0 = (o % (GT / 4)) * 4;
+    const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+    if (out_rows != nullptr) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = h0 + e;
+        if (h < hcnt) {
+          const float L = sL[h];
+          out_rows[(size_t)h * D + d] = __float2half_rn(L > 0.f ? a4[e] / L : 0.f);
+        }
+      }
+    } else {
+      reinterpret_cast<float4*>(out_slot)[o] = acc[i];
+    }
+  }
+  if (gtid < GT) {
+    if (out_slot != nullptr) {
+      out_slot[D * GT + gtid] = sM[gtid];
+      out_slot[D * GT + GT + gtid] = sL[gtid];
+    } else if (gtid < hcnt && !(sL[gtid] > 0.f)) {
+      flag_error(status, PA_ERR_EMPTY_CONTEXT);
+    }
+  }
+  group_sync(bar_id, GS);  // the scratch is reused by the group's next merge
 }
 
 // ---------------------------------------------------------------------------------------
@@ -634,7 +838,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     return pk;
   };
   int cur = batch_info(0);
-  int nxt = batch_info(32);
+  int nxt = 0;  // block ids of pages 32..63: read once the first copies are on their way
 
   auto issue = [&](int j, int s) {
     if (j > 0 && (j & 31) == 0) {
@@ -672,10 +876,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
+  static_assert(DEPTH < 32, "the prologue copies must come from the first batch of block ids");
   const int npro = n < DEPTH ? n : DEPTH;
   __syncwarp();
   for (int j = 0; j < npro; ++j) issue(j, j);
   int issued = npro;
+  nxt = batch_info(32);
   convert_q();
 
   // Shared-memory offsets of the K cells this lane reads (chunk of load si, token of n-tile
@@ -1115,16 +1321,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // ---- 5. Merges of the segments whose last piece this CTA's warps finished ------------------
   // The pieces of a recorded merge are visible: the recording arrival acquired them, and the
   // barrier below orders that arrival before every warp's reads.
-  // Segments with few pieces are merged one per warp, in parallel; larger ones by the whole
-  // CTA together.
+  // Segments with few pieces are merged one per warp, in parallel; larger ones by groups of
+  // four warps, side by side, and only a merge too large for a group's scratch by the whole
+  // CTA.
   if (lane == 0) s_npend[warp] = npend;
   __syncthreads();  // every warp is past its page loop: the ring memory is free scratch
   float* scratch = reinterpret_cast<float*>(k_tiles);
-  // A CTA with many merges runs them one per warp in parallel; one with a few merges runs the
-  // larger of them cooperatively (all warps on one merge). 16-row head tiles keep more
-  // registers per piece and always merge cooperatively.
+  // A CTA with many merges runs them one per warp in parallel; one with a few merges deals
+  // the larger of them to its groups of four warps. 16-row head tiles keep more registers per
+  // piece and never merge in a single warp.
   int n_merges = 0;
   for (int w = 0; w < WARPS; ++w) n_merges += s_npend[w];
+  // Pieces per step of a one-warp merge: four where the launch leaves 255 registers a thread
+  // (8 warps), two under the 168 of 12-warp launches.
+  constexpr int kWarpStep = (WARPS <= 8) ? 4 : 2;
   const int kWarpMerge =
       (GT != 8) ? 0 : (n_merges * 4 >= WARPS ? kWarpMergeMax : 4);
   int idx = 0;
@@ -1139,20 +1349,52 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
       };
       if (a.mode == kModeStream) {
-        warp_combine<D, GT>(piece, np, lane, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
-                            nullptr, a.status);
+        warp_combine<D, GT, kWarpStep>(piece, np, lane, hcnt,
+                                       a.out + ((size_t)b * a.H + hbase) * D, nullptr, a.status);
       } else {
-        warp_combine<D, GT>(piece, np, lane, hcnt, nullptr, a.part_out + (size_t)segid * SLOT,
-                            a.status);
+        warp_combine<D, GT, kWarpStep>(piece, np, lane, hcnt, nullptr,
+                                       a.part_out + (size_t)segid * SLOT, a.status);
       }
       if (lane == 0) a.counters[segid] = 0;
     }
   }
+  constexpr int GS = 128;
+  constexpr int NG = NTHR / GS;
+  constexpr size_t kGroupBytes = (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST) / NG / 16 * 16;
+  const int grp = warp / (GS / 32);
+  int idx_g = 0;
+  bool any_big = false;
+  for (int w = 0; w < WARPS; ++w) {
+    for (int e = 0; e < s_npend[w]; ++e) {
+      const int* pe = s_pend[w][e];
+      const int np = pe[2];
+      if (np <= kWarpMerge) continue;
+      if (Group<D, GT, GS>::floats(np) * sizeof(float) > kGroupBytes) {
+        any_big = true;
+        continue;
+      }
+      if ((idx_g++ % NG) != grp) continue;
+      const int segid = pe[0], wf = pe[1], b = pe[3], hbase = pe[4], hcnt = pe[5];
+      auto piece = [&](int k) -> const float* {
+        return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
+      };
+      const bool stream = (a.mode == kModeStream);
+      group_combine<D, GT, GS>(piece, np, hcnt,
+                               stream ? a.out + ((size_t)b * a.H + hbase) * D : nullptr,
+                               stream ? nullptr : a.part_out + (size_t)segid * SLOT, a.status,
+                               reinterpret_cast<float*>(k_tiles + grp * kGroupBytes),
+                               (int)threadIdx.x - grp * GS, 1 + grp);
+      if ((int)threadIdx.x == grp * GS) a.counters[segid] = 0;
+    }
+  }
+  if (!any_big) return;
+  __syncthreads();  // the groups are done with their parts of the scratch
   for (int w = 0; w < WARPS; ++w) {
     for (int e = 0; e < s_npend[w]; ++e) {
       const int* pe = s_pend[w][e];
       const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
       if (np <= kWarpMerge) continue;
+      if (Group<D, GT, GS>::floats(np) * sizeof(float) <= kGroupBytes) continue;
       if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) >
           (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST)) {
         if (threadIdx.x == 0) flag_error(a.status, PA_ERR_WORKSPACE);

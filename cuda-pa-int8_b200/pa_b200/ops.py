@@ -111,8 +111,18 @@ def _kv_kind(k_cache, k_scales):
 _KV_CODE = {"f16": _lib.PA_DTYPE_F16, "i8": _lib.PA_DTYPE_I8, "f8": _lib.PA_DTYPE_FP8E4M3}
 
 
+def _check_lengths(context_lens, capacity):
+    """The reference's context_lens >= 1 check (and this library's upper bound), from one
+    device-to-host copy of the lengths; synchronises the current stream."""
+    cl = context_lens.cpu()
+    if cl.numel() == 0:
+        return
+    _require(int(cl.min()) >= 1, "context_lens must be >= 1 (empty sequences unsupported)")
+    _require(int(cl.max()) <= capacity, "context_lens exceeds max_blocks_per_seq * block_size")
+
+
 def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
-                       kind, k_scales, v_scales, validate, act_dtype=torch.float16):
+                       kind, k_scales, v_scales, act_dtype=torch.float16):
     scaled = kind != "f16"  # one-byte cache with per-token scales (int8 or fp8)
     _require(q.is_cuda and (out is None or out.is_cuda), "tensors must be on CUDA")
     act_name = "fp16" if act_dtype == torch.float16 else "bf16"
@@ -169,11 +179,6 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
              "block_table must be [num_seqs, max_blocks_per_seq]")
     _require(context_lens.dim() == 1 and context_lens.shape[0] == B,
              "context_lens must be [num_seqs]")
-    if validate and B > 0:
-        mm = torch.stack([context_lens.min(), context_lens.max()]).cpu()
-        _require(int(mm[0]) >= 1, "context_lens must be >= 1 (empty sequences unsupported)")
-        _require(int(mm[1]) <= block_table.shape[1] * block_size,
-                 "context_lens exceeds max_blocks_per_seq * block_size")
     return B, H, KVH, D, NB
 
 
@@ -191,7 +196,7 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
     """
     kind = kv_kind or _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
-                                          block_size, kind, k_scales, v_scales, validate)
+                                          block_size, kind, k_scales, v_scales)
     if B == 0:
         return out
     L = _lib.lib()
@@ -208,16 +213,19 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
                 fn = L.pa_splitk_fp8 if splitk else L.pa_decode_fp8
             else:
                 fn = L.pa_splitk_i8 if splitk else L.pa_decode_i8
-            rc = fn(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            args = (out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                     k_scales.data_ptr(), v_scales.data_ptr(), block_table.data_ptr(),
                     context_lens.data_ptr(), B, H, KVH, D, NB, block_size, max_blocks,
                     float(scale), ws.data_ptr(), ws.numel(), stream)
         else:
             fn = L.pa_splitk_f16 if splitk else L.pa_decode_f16
-            rc = fn(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            args = (out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                     block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D, NB,
                     block_size, max_blocks, float(scale), ws.data_ptr(), ws.numel(), stream)
-        _lib.check(rc, "paged decode")
+        # The one host sync comes last, so the launch follows it with no Python work between.
+        if validate:
+            _check_lengths(context_lens, max_blocks * block_size)
+        _lib.check(fn(*args), "paged decode")
     return out
 
 
@@ -233,7 +241,7 @@ def decode_bf16(out, q, k_cache, v_cache, block_table, context_lens, scale, bloc
     kind = _kv_kind(k_cache, k_scales)
     int8 = kind != "f16"
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
-                                          block_size, kind, k_scales, v_scales, validate,
+                                          block_size, kind, k_scales, v_scales,
                                           act_dtype=torch.bfloat16)
     if B == 0:
         return out
@@ -245,6 +253,8 @@ def decode_bf16(out, q, k_cache, v_cache, block_table, context_lens, scale, bloc
                                                  1 if splitk else 0)
         _require(need > 0, "unsupported decode shape: " + _lib.last_error())
         ws = workspace(q.device, need)
+        if validate:
+            _check_lengths(context_lens, max_blocks * block_size)
         rc = L.pa_decode_bf16q(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(),
                                v_cache.data_ptr(), _ptr(k_scales) if int8 else None,
                                _ptr(v_scales) if int8 else None, block_table.data_ptr(),
@@ -266,7 +276,7 @@ def decode_partial(q, k_cache, v_cache, block_table, context_lens, scale, block_
     partials. Used to split one sequence's context across GPUs."""
     kind = _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(None, q, k_cache, v_cache, block_table, context_lens,
-                                          block_size, kind, k_scales, v_scales, validate=False)
+                                          block_size, kind, k_scales, v_scales)
     per = partial_floats(H, KVH, D) * KVH  # floats per sequence: kv_heads x head tiles x slot
     if partials is None:
         partials = torch.empty(B, per, dtype=torch.float32, device=q.device)

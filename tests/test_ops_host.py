@@ -41,3 +41,12 @@ def test_layout_rejects_mismatches(case):
     with pytest.raises(RuntimeError):
         ops._check_cache_layout(kc, vc, args["num_kv_heads"], args["head_dim"],
                                 args["block_size"], ks, vs)
+
+
+def test_context_length_check():
+    ops._check_lengths(torch.tensor([1, 5, 16], dtype=torch.int32), 16)
+    ops._check_lengths(torch.tensor([], dtype=torch.int32), 16)
+    with pytest.raises(RuntimeError, match=">= 1"):
+        ops._check_lengths(torch.tensor([3, 0], dtype=torch.int32), 16)
+    with pytest.raises(RuntimeError, match="exceeds"):
+        ops._check_lengths(torch.tensor([17, 2], dtype=torch.int32), 16)
