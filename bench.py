@@ -7,7 +7,7 @@ Metric: achieved HBM GB/s of a paged-decode step -- algorithmic 
 Default workload: BASELINE config 2 (FP16, batch 64, context 4096, 32 q / 8 kv heads,
 head_dim 128, block 16, shuffled block tables over 16384 blocks). At N GPUs every rank runs
 its own config-2 batch (sequence sharding, no communication): weak scaling.
-Other configs (parity cases and DESIGN.md numbers): 3 INT8 per-token decode + one-token
+Other configs: 3 INT8 per-token decode + one-token
 quantize-write per sequence (B64, ctx 8192, 12/2); 4 long-context split-K INT8 sharded by
 kv-head (B8, ctx U[65536,131072], 64/8); 5 ragged INT8 serving batch + one-token write per
 sequence, sequences LPT-sharded across ranks (B256, 28/4, ctx lognormal median 2048 sigma 1).

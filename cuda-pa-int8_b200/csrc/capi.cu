@@ -467,6 +467,15 @@ int pa_read_status(void* workspace, int* status_out, void* stream) {
   return PA_OK;
 }
 
+int pa_reset_workspace(void* workspace, size_t workspace_bytes, void* stream) {
+  if (workspace == nullptr || workspace_bytes < sizeof(int))
+    return fail(PA_ERR_INVALID_ARG, "null or empty workspace");
+  const size_t n = workspace_bytes < pa::kWsPartOffset ? workspace_bytes : pa::kWsPartOffset;
+  cudaError_t e = cudaMemsetAsync(workspace, 0, n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "workspace reset");
+  return PA_OK;
+}
+
 int pa_decode_f16(void* out, const void* q, const void* k_cache, const void* v_cache,
                   const int32_t* block_table, const int32_t* context_lens, int num_seqs,
                   int num_heads, int num_kv_heads, int head_dim, int num_blocks, int block_size,

@@ -1397,7 +1397,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       if (Group<D, GT, GS>::floats(np) * sizeof(float) <= kGroupBytes) continue;
       if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) >
           (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST)) {
-        if (threadIdx.x == 0) flag_error(a.status, PA_ERR_WORKSPACE);
+        if (threadIdx.x == 0) {
+          flag_error(a.status, PA_ERR_WORKSPACE);
+          a.counters[segid] = 0;  // leave the counter ready for the next call
+        }
         continue;
       }
       auto piece = [&](int k) -> const float* {

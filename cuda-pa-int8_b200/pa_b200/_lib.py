@@ -46,6 +46,7 @@ SIGNATURES = {
     "pa_status_string": (ctypes.c_char_p, [_i]),
     "pa_decode_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
     "pa_read_status": (_i, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
+    "pa_reset_workspace": (_i, [_vp, _sz, _vp]),
     "pa_decode_f16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp,
                            _sz, _vp]),
     "pa_decode_i8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
@@ -54,6 +55,7 @@ SIGNATURES = {
                            _sz, _vp]),
     "pa_decode_f16_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
                                    _vp]),
+    "pa_decode_f16_noalloc_read_status": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
     "pa_splitk_i8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f,
                           _vp, _sz, _vp]),
     "pa_decode_bf16q_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),

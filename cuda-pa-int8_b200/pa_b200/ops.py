@@ -52,15 +52,21 @@ def workspace(device, nbytes):
 
 def read_status(device=None):
     """OR of the device status words of this device's workspaces, which are then cleared
-    (synchronises). Bits are the PA_ERR_* codes of include/pa_b200.h."""
+    (synchronises). Bits are the PA_ERR_* codes of include/pa_b200.h. A workspace that
+    reports an error also gets its arrival counters zeroed, since a kernel that stopped
+    part-way can leave some of them set."""
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
     status = 0
+    L = _lib.lib()
     for (idx, stream), ws in list(_workspaces.items()):
         if idx != device.index:
             continue
         out = ctypes.c_int(0)
-        _lib.check(_lib.lib().pa_read_status(ws.data_ptr(), ctypes.byref(out), stream),
-                   "pa_read_status")
+        _lib.check(L.pa_read_status(ws.data_ptr(), ctypes.byref(out), stream), "pa_read_status")
+        if out.value:
+            _lib.check(L.pa_reset_workspace(ws.data_ptr(), ws.numel(), stream),
+                       "pa_reset_workspace")
+            torch.cuda.synchronize(device)
         status |= out.value
     return status
 

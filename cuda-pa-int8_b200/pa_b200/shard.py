@@ -63,22 +63,44 @@ class SplitContextDecode:
     step(out, q, ...) runs the local partial decode, all-gathers the partials over the
     process group and merges them; every rank ends with the full output. The collective is
     the only cross-GPU traffic: num_seqs * num_kv_heads * slot floats per rank.
+
+    partial_fn and merge_fn default to the CUDA ops (ops.decode_partial, ops.merge_partials);
+    they take the same arguments as those, so the exchange itself can be driven with other
+    implementations of the two steps (the CPU tests pass the oracle's).
     """
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, partial_fn=None, merge_fn=None):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
+        if partial_fn is None or merge_fn is None:
+            from . import ops
+            partial_fn = partial_fn or ops.decode_partial
+            merge_fn = merge_fn or ops.merge_partials
+        self.partial_fn = partial_fn
+        self.merge_fn = merge_fn
+        self._gathered = None
+
+    def gather_buffer(self, part):
+        """The [world * num_seqs, per_seq] receive buffer for partials shaped like `part`,
+        kept between steps (so a captured step keeps its address)."""
+        import torch
+        shape = (self.world * part.shape[0],) + tuple(part.shape[1:])
+        g = self._gathered
+        if g is None or tuple(g.shape) != shape or g.device != part.device:
+            g = torch.empty(shape, dtype=part.dtype, device=part.device)
+            self._gathered = g
+        return g
 
     def step(self, out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16,
              k_scales=None, v_scales=None):
-        import torch
-        from . import ops
-        part = ops.decode_partial(q, k_cache, v_cache, block_table, context_lens, scale,
-                                  block_size, k_scales=k_scales, v_scales=v_scales)
-        gathered = torch.empty((self.world,) + tuple(part.shape), dtype=part.dtype,
-                               device=part.device)
+        part = self.partial_fn(q, k_cache, v_cache, block_table, context_lens, scale,
+                               block_size, k_scales=k_scales, v_scales=v_scales)
+        # Gathered along dim 0 ([world * num_seqs, per]: the layout every backend accepts),
+        # then viewed as [world, num_seqs, per] for the merge.
+        gathered = self.gather_buffer(part)
         self.dist.all_gather_into_tensor(gathered, part, group=self.group)
-        ops.merge_partials(out, gathered, q.shape[1], k_cache.shape[1])
+        self.merge_fn(out, gathered.view((self.world,) + tuple(part.shape)), q.shape[1],
+                      k_cache.shape[1])
         return out

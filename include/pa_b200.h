@@ -79,6 +79,12 @@ size_t pa_decode_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, 
 /* Read the device status word of a workspace (synchronises `stream`), then clear it. */
 int pa_read_status(void* workspace, int* status_out, void* stream);
 
+/* Zero a workspace's status word and arrival counters (its first min(workspace_bytes,
+ * 256 B + 1 MiB) bytes) on `stream`. A decode that stopped part-way on a device error (a
+ * wait that gave up) can leave counters set, so after pa_read_status reports a nonzero status
+ * call this before the next decode on that workspace. The reference has no workspace. */
+int pa_reset_workspace(void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Single-pass decode, FP16 KV cache: one launch, fused cross-split log-sum-exp combine.
  * Replaces the launchers behind paged_decode_attention / paged_decode_attn_{vec,online,warp}
@@ -140,11 +146,19 @@ int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_c
  * shapes whose scratch exceeds it (more than 8 q heads per kv head) are rejected with
  * PA_ERR_WORKSPACE. The first call on a device looks up the array's address and should come
  * before any stream capture. Calls share the array: calls that overlap on the GPU race, so
- * order them on one stream. This entry point has no counterpart in the reference. */
+ * order them on one stream. Device-side errors (bad context length, bad block id, a wait
+ * that gave up) accumulate in the array's status word until
+ * pa_decode_f16_noalloc_read_status reads and clears them. This entry point has no
+ * counterpart in the reference. */
 int pa_decode_f16_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
                           const int32_t* block_table, const int32_t* context_lens, int num_seqs,
                           int num_heads, int num_kv_heads, int head_dim, int num_blocks,
                           int block_size, int max_blocks_per_seq, float scale, void* stream);
+
+/* Read the device status word of pa_decode_f16_noalloc's static scratch on the current
+ * device (synchronises `stream`), then clear it; the PA_ERR_* bits of every call since the
+ * last read. No counterpart in the reference. */
+int pa_decode_f16_noalloc_read_status(int* status_out, void* stream);
 
 /* Decode with bf16 activations: q and out are bf16 [num_seqs, num_heads, head_dim]; the cache
  * is fp16 (kv_dtype PA_DTYPE_F16), per-token int8 (PA_DTYPE_I8) or per-token fp8 e4m3

@@ -268,6 +268,63 @@ def range_partials(q, k_cache, v_cache, block_table, context_lens, t_lo, t_hi, s
     return m, l, acc
 
 
+LOG2E = 1.4426950408889634
+
+
+def _slot_shape(num_heads, num_kv_heads, head_dim=128):
+    G = num_heads // num_kv_heads
+    GT = 8 if G <= 8 else 16
+    HT = -(-G // GT)
+    return G, GT, HT, (head_dim + 2) * GT
+
+
+def pack_slots(m, l, acc, num_kv_heads):
+    """Partials (m, l [S, H] natural-log units, acc [S, H, D]) in the slot layout the CUDA
+    partial decode writes: fp32 [S, num_kv_heads * head_tiles * slot], a slot per (kv head,
+    head tile) holding O[D][GT], then m[GT] in log2 units, then l[GT]; head rows past the
+    group are empty (m = -inf, l = 0)."""
+    S, H, D = acc.shape
+    G, GT, HT, SLOT = _slot_shape(H, num_kv_heads, D)
+    out = np.zeros((S, num_kv_heads * HT, SLOT), np.float32)
+    for kvh in range(num_kv_heads):
+        for ht in range(HT):
+            seg = kvh * HT + ht
+            o = np.zeros((S, D, GT), np.float32)
+            mm = np.full((S, GT), -np.inf, np.float32)
+            ll = np.zeros((S, GT), np.float32)
+            for h in range(min(GT, G - ht * GT)):
+                qh = kvh * G + ht * GT + h
+                o[:, :, h] = acc[:, qh, :]
+                mm[:, h] = m[:, qh] * LOG2E
+                ll[:, h] = l[:, qh]
+            out[:, seg, :D * GT] = o.reshape(S, D * GT)
+            out[:, seg, D * GT:D * GT + GT] = mm
+            out[:, seg, D * GT + GT:] = ll
+    return out.reshape(S, -1)
+
+
+def unpack_slots(slots, num_heads, num_kv_heads, head_dim=128):
+    """Inverse of pack_slots: (m, l, acc) in natural-log units from [..., S, per_seq]."""
+    slots = np.asarray(slots, np.float64)
+    lead = slots.shape[:-1]
+    G, GT, HT, SLOT = _slot_shape(num_heads, num_kv_heads, head_dim)
+    x = slots.reshape(lead + (num_kv_heads * HT, SLOT))
+    D = head_dim
+    m = np.full(lead + (num_heads,), -np.inf)
+    l = np.zeros(lead + (num_heads,))
+    acc = np.zeros(lead + (num_heads, D))
+    for kvh in range(num_kv_heads):
+        for ht in range(HT):
+            seg = x[..., kvh * HT + ht, :]
+            o = seg[..., :D * GT].reshape(lead + (D, GT))
+            for h in range(min(GT, G - ht * GT)):
+                qh = kvh * G + ht * GT + h
+                acc[..., qh, :] = o[..., :, h]
+                m[..., qh] = seg[..., D * GT + h] / LOG2E
+                l[..., qh] = seg[..., D * GT + GT + h]
+    return m, l, acc
+
+
 def lse_merge(ms, ls, accs):
     """Merge partials stacked on axis 0: out = sum acc_s e^{m_s-M} / sum l_s e^{m_s-M}."""
     ms, ls, accs = np.asarray(ms), np.asarray(ls), np.asarray(accs)

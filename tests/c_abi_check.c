@@ -55,6 +55,8 @@ int main(void) {
                         (const int32_t*)fake(), 1, 8, 2, 128, 4, 16, 2, PA_DTYPE_F32, 0, 0.1f,
                         fake(), (size_t)1 << 30, NULL) == PA_ERR_UNSUPPORTED);
   CHECK(pa_selftest_bounded_wait(NULL, NULL) == PA_ERR_INVALID_ARG);
+  CHECK(pa_reset_workspace(NULL, 1024, NULL) == PA_ERR_INVALID_ARG);
+  CHECK(pa_decode_f16_noalloc_read_status(NULL, NULL) == PA_ERR_INVALID_ARG);
   CHECK(pa_partial_floats(12, 2, 128) == 130 * 8);
   CHECK(pa_partial_floats(12, 5, 128) == 0);
 

@@ -84,7 +84,8 @@ def test_extension_entry_points_check_arguments_on_the_host(lib):
     names = set(_declared())
     for must in ("pa_decode_fp8", "pa_splitk_fp8", "pa_quantize_into_cache_fp8",
                  "pa_decode_bf16q", "pa_decode_bf16q_workspace_bytes",
-                 "pa_selftest_bounded_wait", "pa_decode_f16_noalloc"):
+                 "pa_selftest_bounded_wait", "pa_decode_f16_noalloc",
+                 "pa_decode_f16_noalloc_read_status", "pa_reset_workspace"):
         assert must in names
     assert b"fp16 range" in lib.pa_status_string(_lib.PA_ERR_Q_RANGE)
     p = 1 << 20
@@ -106,8 +107,10 @@ def test_extension_entry_points_check_arguments_on_the_host(lib):
     rc = lib.pa_quantize_into_cache_fp8(p, p, _lib.PA_DTYPE_F16, 256, p, 4, 2, 128, p, p, None, p,
                                         4, 16, None, None)
     assert rc == _lib.PA_ERR_INVALID_ARG
-    # the wait self-test needs a status word
+    # the wait self-test needs a status word; reset and status reads need their buffers
     assert lib.pa_selftest_bounded_wait(None, None) == _lib.PA_ERR_INVALID_ARG
+    assert lib.pa_reset_workspace(None, 1024, None) == _lib.PA_ERR_INVALID_ARG
+    assert lib.pa_decode_f16_noalloc_read_status(None, None) == _lib.PA_ERR_INVALID_ARG
 
 
 def test_plain_c_caller(lib, tmp_path):

@@ -1,5 +1,6 @@
-"""CPU: multi-GPU sharding logic (pa_b200.shard) and the cross-rank split-context exchange,
-run as world-size-2 gloo process groups with the oracle standing in for the GPU kernels."""
+"""CPU: multi-GPU sharding logic (pa_b200.shard) and the cross-rank split-context exchange
+(shard.SplitContextDecode.step itself), run as world-size-2 gloo process groups with the
+oracle standing in for the two GPU kernels of the step."""
 
 import os
 import socket
@@ -63,15 +64,47 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _split_context_worker(rank, world, port, result_q):
+def _oracle_partial(q, k_cache, v_cache, block_table, context_lens, scale, block_size=16,
+                    k_scales=None, v_scales=None):
+    """The partial decode step of SplitContextDecode, computed by the oracle on CPU tensors
+    and returned in the CUDA kernel's slot layout."""
+    kc, vc = k_cache.numpy(), v_cache.numpy()
+    if k_scales is not None:
+        kc, vc = pa_oracle.dequantize_kv(kc, vc, k_scales.numpy(), v_scales.numpy())
+    cl = context_lens.numpy()
+    m, l, acc = pa_oracle.range_partials(q.numpy(), kc, vc, block_table.numpy(), cl,
+                                         np.zeros_like(cl), cl, scale)
+    return torch.from_numpy(pa_oracle.pack_slots(m, l, acc, k_cache.shape[1]))
+
+
+def _oracle_merge(out, gathered, num_heads, num_kv_heads):
+    """The merge step: [world, num_seqs, per_seq] partials -> fp16 out, by the oracle."""
+    assert gathered.dim() == 3
+    m, l, acc = pa_oracle.unpack_slots(gathered.numpy(), num_heads, num_kv_heads)
+    out.copy_(torch.from_numpy(pa_oracle.lse_merge(m, l, acc)).to(out.dtype))
+    return out
+
+
+def _split_context_worker(rank, world, port, int8, result_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         lens = [700, 33, 1, 1500]
-        c = gen.decode_case(seed=41, num_seqs=4, num_heads=8, num_kv_heads=2, context_lens=lens)
+        H, KVH = 12, 2
+        c = gen.decode_case(seed=41, num_seqs=4, num_heads=H, num_kv_heads=KVH,
+                            context_lens=lens)
         kc, vc = pa_oracle.scatter_paged_cache(c["k"], c["v"], c["context_lens"],
                                                c["block_table"], c["num_blocks"])
+        ks = vs = None
+        if int8:
+            kq, ksc = pa_oracle.quantize_per_token(c["k"], "f16")
+            vq, vsc = pa_oracle.quantize_per_token(c["v"], "f16")
+            nb = c["num_blocks"]
+            kc, vc = pa_oracle.scatter_paged_cache(kq, vq, c["context_lens"], c["block_table"],
+                                                   nb)
+            ks = pa_oracle.scatter_scales(ksc, c["context_lens"], c["block_table"], nb, KVH)
+            vs = pa_oracle.scatter_scales(vsc, c["context_lens"], c["block_table"], nb, KVH)
         scale = 1 / np.sqrt(128)
         # This rank's share: block ids and context length of its token range per sequence.
         S = len(lens)
@@ -81,37 +114,54 @@ def _split_context_worker(rank, world, port, result_q):
             blocks, n = shard.local_view(c["block_table"][b], lens[b], world, rank)
             bt_local[b, :len(blocks)] = blocks
             cl_local[b] = n
-        m, l, acc = pa_oracle.range_partials(c["q"], kc, vc, bt_local, cl_local,
-                                             np.zeros(S, np.int32), cl_local, scale)
-        local = torch.from_numpy(np.concatenate([m.ravel(), l.ravel(), acc.ravel()]))
-        gathered = [torch.empty_like(local) for _ in range(world)]
-        dist.all_gather(gathered, local)
-        H, D = 8, 128
-        ms = np.stack([g[:S * H].numpy().reshape(S, H) for g in gathered])
-        ls = np.stack([g[S * H:2 * S * H].numpy().reshape(S, H) for g in gathered])
-        accs = np.stack([g[2 * S * H:].numpy().reshape(S, H, D) for g in gathered])
-        merged = pa_oracle.lse_merge(ms, ls, accs)
+        dec = shard.SplitContextDecode(partial_fn=_oracle_partial, merge_fn=_oracle_merge)
+        out = torch.empty(S, H, 128, dtype=torch.float16)
+        t = torch.from_numpy
+        dec.step(out, t(c["q"]), t(kc), t(vc), t(bt_local), t(cl_local), scale, 16,
+                 k_scales=None if ks is None else t(ks), v_scales=None if vs is None else t(vs))
+        if int8:
+            kc, vc = pa_oracle.dequantize_kv(kc, vc, ks, vs)
         full = pa_oracle.paged_decode_attention(c["q"], kc, vc, c["block_table"],
                                                 c["context_lens"], scale=scale)
-        result_q.put((rank, float(np.abs(merged - full).max())))
+        result_q.put((rank, float(np.abs(out.float().numpy() - full).max())))
     finally:
         dist.destroy_process_group()
 
 
-def test_split_context_exchange_gloo_world2():
-    """Two ranks each own a block-aligned half of every sequence; their partials, exchanged
-    with all_gather and LSE-merged, equal the one-pass decode."""
+@pytest.mark.parametrize("int8", [False, True])
+def test_split_context_exchange_gloo_world2(int8):
+    """Two ranks each own a block-aligned half of every sequence and run
+    SplitContextDecode.step: local partials, all_gather over the process group, LSE merge. The
+    result on every rank equals the one-pass decode (fp16 output rounding)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_split_context_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_split_context_worker, args=(r, 2, port, int8, q))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = sorted(q.get(timeout=5) for _ in range(2))
-    assert all(err < 1e-5 for _, err in res), res
+    assert all(err < 1e-3 for _, err in res), res
+
+
+def test_slot_packing_round_trips():
+    rng = np.random.default_rng(3)
+    for H, KVH in ((12, 2), (8, 8), (40, 2), (7, 1)):
+        S = 3
+        m = rng.standard_normal((S, H))
+        l = rng.random((S, H)) + 0.5
+        acc = rng.standard_normal((S, H, 128))
+        slots = pa_oracle.pack_slots(m, l, acc, KVH)
+        G = H // KVH
+        GT = 8 if G <= 8 else 16
+        assert slots.shape == (S, KVH * -(-G // GT) * 130 * GT)
+        m2, l2, a2 = pa_oracle.unpack_slots(slots, H, KVH)
+        np.testing.assert_allclose(m2, m, rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(l2, l, rtol=1e-6)
+        np.testing.assert_allclose(a2, acc, rtol=1e-6, atol=1e-6)
 
 
 def _dead_peer_worker(rank, world, port, result_q):
