@@ -71,9 +71,10 @@ class SplitContextDecode:
 
     def __init__(self, group=None, partial_fn=None, merge_fn=None):
         import torch.distributed as dist
-        self.dist = dist
+        # Without an initialised process group the step runs on one rank: the gather is a copy.
+        self.dist = dist if (dist.is_available() and dist.is_initialized()) else None
         self.group = group
-        self.world = dist.get_world_size(group)
+        self.world = self.dist.get_world_size(group) if self.dist else 1
         if partial_fn is None or merge_fn is None:
             from . import ops
             partial_fn = partial_fn or ops.decode_partial
@@ -100,7 +101,10 @@ class SplitContextDecode:
         # Gathered along dim 0 ([world * num_seqs, per]: the layout every backend accepts),
         # then viewed as [world, num_seqs, per] for the merge.
         gathered = self.gather_buffer(part)
-        self.dist.all_gather_into_tensor(gathered, part, group=self.group)
+        if self.dist is not None:
+            self.dist.all_gather_into_tensor(gathered, part, group=self.group)
+        else:
+            gathered.copy_(part)
         self.merge_fn(out, gathered.view((self.world,) + tuple(part.shape)), q.shape[1],
                       k_cache.shape[1])
         return out

@@ -201,3 +201,20 @@ def test_split_context_exchange_reports_a_dead_peer():
     assert procs[0].exitcode == 0, procs[0].exitcode
     rank, outcome = q.get(timeout=5)
     assert rank == 0 and outcome.startswith("error"), outcome
+
+
+def test_split_context_single_rank_without_process_group():
+    """With no process group the step runs on one rank (the gather is a copy)."""
+    assert not dist.is_initialized()
+    lens = [300, 17]
+    c = gen.decode_case(seed=8, num_seqs=2, num_heads=8, num_kv_heads=2, context_lens=lens)
+    kc, vc = pa_oracle.scatter_paged_cache(c["k"], c["v"], c["context_lens"], c["block_table"],
+                                           c["num_blocks"])
+    dec = shard.SplitContextDecode(partial_fn=_oracle_partial, merge_fn=_oracle_merge)
+    assert dec.world == 1
+    out = torch.empty(2, 8, 128, dtype=torch.float16)
+    t = torch.from_numpy
+    dec.step(out, t(c["q"]), t(kc), t(vc), t(c["block_table"]), t(c["context_lens"]),
+             1 / np.sqrt(128))
+    full = pa_oracle.paged_decode_attention(c["q"], kc, vc, c["block_table"], c["context_lens"])
+    assert float(np.abs(out.float().numpy() - full).max()) < 1e-3
