@@ -297,10 +297,7 @@ def build_workload(torch, name, rank, world, device):
             fill(k, v, bt[b0:b1], lens[b0:b1])
             del k, v
     if w.step_tokens:
-        # The token written each step: slot of position lens[b] in sequence b.
-        pos = torch.from_numpy(lens.astype(np.int64)).to(device)
-        blk = bt.gather(1, (pos // BLOCK).view(-1, 1)).view(-1).long()
-        w.slots = (blk * BLOCK + pos % BLOCK).to(torch.int32)
+        # The token written each step, at position lens[b] (context_lens[b] - 1).
         w.new_k = _kv_rows(torch, (B, KVH, HEAD_DIM), spec["dist"], gen, device)
         w.new_v = _kv_rows(torch, (B, KVH, HEAD_DIM), spec["dist"], gen, device)
     per_tok = KVH * (2 * HEAD_DIM * (2 if w.kv == "f16" else 1) + (0 if w.kv == "f16" else 8))
@@ -337,18 +334,14 @@ def make_step(w, splitk=False, validate=False, decode_only=False):
         dec_launches = 2 if use_split else 1
 
     if w.step_tokens and not decode_only:
-        def write():
-            if w.kv == "f16":
-                ops.write_into_cache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.slots, BLOCK)
-            else:
-                ops.quantize_into_cache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.k_scales,
-                                        w.v_scales, w.slots, BLOCK, k_scale=w.k_fix,
-                                        v_scale=w.v_fix)
-
+        # The decode step API: the new token of every sequence is written into the cache by
+        # the decode kernel itself (one launch; the split-K pair adds its reduce).
         def step():
-            write()
-            decode()
-        return step, 1 + dec_launches
+            ops.decode_step(w.out, w.q, w.new_k, w.new_v, w.k_cache, w.v_cache, w.block_table,
+                            w.context_lens, scale, BLOCK, k_scales=w.k_scales,
+                            v_scales=w.v_scales, k_scale=w.k_fix, v_scale=w.v_fix,
+                            splitk=use_split, validate=validate)
+        return step, dec_launches
     return decode, dec_launches
 
 
@@ -826,13 +819,12 @@ def e2e_measure(torch, w, args, dist, device, total_bytes, total_seqs):
         dq.copy_(hq, non_blocking=True)
         dbt.copy_(hbt, non_blocking=True)
         dcl.copy_(hcl, non_blocking=True)
-        if w.step_tokens and w.kv == "f16":
-            ops.write_into_cache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.slots, BLOCK)
-        elif w.step_tokens:
-            ops.quantize_into_cache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.k_scales,
-                                    w.v_scales, w.slots, BLOCK, k_scale=w.k_fix,
-                                    v_scale=w.v_fix)
-        if w.kv == "f8":
+        if w.step_tokens:
+            # A decode step: the library's step API (the reference has no batched step op).
+            ops.decode_step(dout, dq, w.new_k, w.new_v, w.k_cache, w.v_cache, dbt, dcl, scale,
+                            BLOCK, k_scales=w.k_scales, v_scales=w.v_scales, k_scale=w.k_fix,
+                            v_scale=w.v_fix, splitk=args.splitk or w.splitk)
+        elif w.kv == "f8":
             # No reference op takes an FP8 cache: the library's own decode op.
             ops.decode(dout, dq, w.k_cache, w.v_cache, dbt, dcl, scale, BLOCK,
                        k_scales=w.k_scales, v_scales=w.v_scales, splitk=args.splitk)
@@ -860,7 +852,8 @@ def e2e_measure(torch, w, args, dist, device, total_bytes, total_seqs):
     return {"value": total_bytes / e2e_s / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "seqs_per_s": total_seqs / e2e_s, "ms_per_step": e2e_s * 1e3,
-            "path": ("pa_b200.ops.decode" if w.kv == "f8" else "pa_b200.cuda_ext") +
+            "path": ("pa_b200.ops.decode_step" if w.step_tokens else
+                     "pa_b200.ops.decode" if w.kv == "f8" else "pa_b200.cuda_ext") +
                     " (validate=True: one context_lens host check/step)"}
 
 

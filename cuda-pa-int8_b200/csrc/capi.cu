@@ -256,11 +256,24 @@ size_t ws_bytes_for(const Shape& s, int mode, int B) {
   return off + parts;
 }
 
+// The new token of a decode step (pa_decode_step): rows, their dtype, the optional per-tensor
+// scales, and whether the decode kernel may write it itself.
+struct StepWrite {
+  const void* k;
+  const void* v;
+  int dtype;
+  long long stride;  // elements per token
+  const float* kfix;
+  const float* vfix;
+  bool fused;
+};
+
 int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
                 const void* k_cache, const void* v_cache, const float* k_scales,
                 const float* v_scales, const int32_t* block_table, const int32_t* context_lens,
                 int B, int H, int KVH, int D, int NB, int bs, int max_blocks, float scale,
-                void* workspace, size_t workspace_bytes, void* stream) {
+                void* workspace, size_t workspace_bytes, void* stream,
+                const StepWrite* sw = nullptr) {
   int rc = check_common(B, H, KVH, D, NB, bs, max_blocks);
   if (rc != PA_OK) return rc;
   if (B == 0) return PA_OK;
@@ -306,6 +319,20 @@ int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
   float* part = reinterpret_cast<float*>(ws + pa::kWsPartOffset);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
+  // A decode step writes its new tokens first: inside the decode kernel when exactly one warp
+  // reads each page (one head tile per kv head), else as its own launch before the decode.
+  const int row_kind = kv_i8 == 1 ? pa::kRowsI8 : (kv_i8 == 2 ? pa::kRowsFP8 : pa::kRowsF16);
+  const bool fuse = sw != nullptr && sw->fused && s.HT == 1;
+  if (sw != nullptr && !fuse) {
+    cudaError_t e = pa::launch_step_rows(
+        sw->dtype, row_kind, sw->k, sw->v, sw->stride, block_table, context_lens, max_blocks, B,
+        KVH, const_cast<void*>(k_cache), const_cast<void*>(v_cache),
+        const_cast<float*>(k_scales), const_cast<float*>(v_scales), NB, bs, sw->kfix, sw->vfix,
+        status, st);
+    if (e != cudaSuccess) return cuda_fail(e, "step write launch");
+  }
+  const size_t new_es = sw == nullptr ? 0 : (sw->dtype == PA_DTYPE_F32 ? 4 : 2);
+
   for (int c0 = 0; c0 < B; c0 += s.chunk_b) {
     const int nb = (B - c0) < s.chunk_b ? (B - c0) : s.chunk_b;
     pa::DecodeArgs a;
@@ -334,6 +361,18 @@ int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
     a.s_max = s.s_max;
     a.bulk = bulk ? 1 : 0;
     a.qk_scale_log2 = scale * 1.4426950408889634f;
+    if (fuse) {
+      a.new_k = static_cast<const uint8_t*>(sw->k) + (size_t)c0 * sw->stride * new_es;
+      a.new_v = static_cast<const uint8_t*>(sw->v) + (size_t)c0 * sw->stride * new_es;
+      a.new_dtype = sw->dtype;
+      a.new_stride = sw->stride;
+      a.new_kfix = sw->kfix;
+      a.new_vfix = sw->vfix;
+      a.kc_w = const_cast<void*>(k_cache);
+      a.vc_w = const_cast<void*>(v_cache);
+      a.ks_w = const_cast<float*>(k_scales);
+      a.vs_w = const_cast<float*>(v_scales);
+    }
     // Grid: one CTA per SM; fewer only when there are fewer subpages than warps.
     const long long subpages = ((long long)max_blocks * bs + pa::kSubTokens - 1) / pa::kSubTokens;
     const long long t_max = (long long)nb * s.SEGS * subpages;
@@ -616,6 +655,40 @@ int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_c
                      block_table, context_lens, num_seqs, num_heads, num_kv_heads, head_dim,
                      num_blocks, block_size, max_blocks_per_seq, scale, workspace,
                      workspace_bytes, stream);
+}
+
+int pa_decode_step(int kv_dtype, void* out, const void* q, const void* new_k,
+                   const void* new_v, int new_dtype, int64_t new_token_stride, void* k_cache,
+                   void* v_cache, float* k_scales, float* v_scales, const float* k_fixed_scale,
+                   const float* v_fixed_scale, const int32_t* block_table,
+                   const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                   int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                   float scale, int splitk, int fused, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  const NvtxRange nvtx_range("pa_decode_step");
+  const int kind = kv_kind(kv_dtype);
+  if (kind < 0)
+    return fail(PA_ERR_UNSUPPORTED,
+                "kv_dtype must be PA_DTYPE_F16, PA_DTYPE_I8 or PA_DTYPE_FP8E4M3");
+  int rc = check_in_dtype(new_dtype);
+  if (rc != PA_OK) return rc;
+  if (num_seqs == 0) return PA_OK;
+  if (new_k == nullptr || new_v == nullptr)
+    return fail(PA_ERR_INVALID_ARG, "null new-token pointer");
+  if (num_kv_heads <= 0 || new_token_stride < (int64_t)num_kv_heads * head_dim)
+    return fail(PA_ERR_INVALID_ARG, "new_token_stride smaller than num_kv_heads*head_dim");
+  const size_t es = (size_t)elem_size(new_dtype);
+  if (!aligned(new_k, es * 4) || !aligned(new_v, es * 4) || new_token_stride % 4 != 0)
+    return fail(PA_ERR_INVALID_ARG, "misaligned new-token rows");
+  if ((k_fixed_scale != nullptr || v_fixed_scale != nullptr) &&
+      (kind != 1 || k_fixed_scale == nullptr || v_fixed_scale == nullptr))
+    return fail(PA_ERR_INVALID_ARG, "fixed scales need an int8 cache and both of k and v");
+  StepWrite sw{new_k, new_v, new_dtype, (long long)new_token_stride, k_fixed_scale,
+               v_fixed_scale, fused != 0};
+  return decode_impl(splitk ? pa::kModeSplit : pa::kModeStream, kind, out, nullptr, q, k_cache,
+                     v_cache, k_scales, v_scales, block_table, context_lens, num_seqs,
+                     num_heads, num_kv_heads, head_dim, num_blocks, block_size,
+                     max_blocks_per_seq, scale, workspace, workspace_bytes, stream, &sw);
 }
 
 int pa_partial_floats(int num_heads, int num_kv_heads, int head_dim) {

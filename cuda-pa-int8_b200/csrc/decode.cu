@@ -18,13 +18,13 @@
 //    (the split-K pair); partial mode writes one merged partial per segment (cross-GPU).
 //  * All q heads of a GQA group share one pass over the K/V page: QK^T and PV run on the
 //    tensor cores (mma.sync m16n8k16, f16 in / f32 accumulate) with heads on the MMA rows
-//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8: QK runs on
-//    the integer tensor cores (m16n8k32) on the raw K bytes against q split into two int8
-//    parts; V bytes are unpacked to exact fp16 integers in registers. FP8: K and V bytes
-//    convert to fp16 exactly in registers (hardware e4m3x2 -> f16x2). For both, the
-//    per-token K scale multiplies the dot product and the per-token V scale is folded into
-//    the softmax weight (the dequant fusion of kernels/paged_attention_v5_warp_int8.cu:
-//    82-85,101-108).
+//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8 and FP8 K/V
+//    bytes convert to fp16 exactly in registers (int8: magic-exponent unpack; e4m3: hardware
+//    e4m3x2 -> f16x2), so every QK product is exact. The per-token K scale multiplies the
+//    dot product and the per-token V scale is folded into the softmax weight (the dequant
+//    fusion of kernels/paged_attention_v5_warp_int8.cu:82-85,101-108); the weights enter the
+//    PV MMA as two fp16 parts (hi + lo), so the output tracks the reference's fp32 arithmetic
+//    to about 1e-5 even where attention concentrates on a few large V entries.
 //
 // Arithmetic follows the reference decode (tests/paged_decode_attn.py:4-49 and the split-K
 // pair kernels/paged_attention_v4_splitk.cu:28-187): softmax(scale * q.k) v over the tokens
@@ -34,6 +34,7 @@
 
 #include "pa_common.cuh"
 #include "pa_internal.h"
+#include "pa_rows.cuh"
 
 #include <atomic>
 #include <cstdio>
@@ -52,6 +53,11 @@ __device__ __forceinline__ int chunk_f16(int r, int si) { return r + 4 * si; }
 
 // Offset of the 16 V scales inside an INT8 stage's scale tile (K scales sit at 0).
 constexpr int kVsOff = 128;
+
+// log2 of the factor by which the decode loop forms its softmax weights (2^6): large enough
+// to keep the hi/lo fp16 parts of the weights normal, small enough that weight x V scale stays
+// below the fp16 maximum for any fp16-derived scale (V scale <= 65504 / 127).
+constexpr float kPExp = 6.f;
 
 template <int KVK, int D, int GT, int DEPTH, int WARPS>
 struct Tile {
@@ -600,6 +606,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     prefetch_l2_share(a.block_table, (size_t)a.B * a.max_blocks * sizeof(int), blockIdx.x,
                       gridDim.x);
     prefetch_l2_share(a.q, (size_t)a.B * a.H * D * sizeof(__half), blockIdx.x, gridDim.x);
+    if (a.new_k != nullptr) {
+      const size_t nb = (size_t)a.B * a.new_stride * (a.new_dtype == PA_DTYPE_F32 ? 4 : 2);
+      prefetch_l2_share(a.new_k, nb, blockIdx.x, gridDim.x);
+      prefetch_l2_share(a.new_v, nb, blockIdx.x, gridDim.x);
+    }
     prefetch_tensormap(&tm_k);
     if (!a.bulk) {
       prefetch_tensormap(&tm_v);
@@ -730,13 +741,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   int cctx = s_ctx[cb];
   const float qs = a.qk_scale_log2;
 
-  // Q fragments. FP16 cache: fp16 A fragments of the m16n8k16 MMA (qa rows g, qb rows g+8).
-  // INT8 cache: each q row is split into two int8 parts, q ~ qsc * (q1 + q2 / 254) (error at
-  // most qsc / 508 per element), held as A fragments of the integer m16n8k32 MMA, so raw K
-  // bytes feed the tensor cores with no unpacking: x = {q1 lo, q1 hi, q2 lo, q2 hi}.
+  // Q fragments: fp16 A fragments of the m16n8k16 MMA (qa rows g, qb rows g+8), loaded in
+  // the chunk order of the cache's K tile layout. K is fp16 in every QK product (int8 and e4m3
+  // bytes convert to fp16 exactly), so the products are exact and sum in fp32, as in the
+  // reference's fp32 dequantised attention.
   uint4 qa[NS], qb[NS];
-  uint4 ra[NS], rb[NS];  // raw fp16 q rows, fetched ahead of their conversion
-  float qsc0 = 0.f, qsc1 = 0.f;
+  uint4 ra[NS], rb[NS];  // q rows fetched ahead of the piece that uses them
   int q_b = -1, q_seg = -1;
 
   auto fetch_q = [&](int b, int seg) {
@@ -757,58 +767,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   };
-  auto split_row = [&](const uint4 (&src)[NS], uint4 (&dst)[NS], float& qsc) {
-    float amax = 0.f;
-#pragma unroll
-    for (int si = 0; si < NS; ++si) {
-      const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
-        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-      }
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    qsc = amax * (1.f / 127.f);
-    const float inv = amax > 0.f ? 127.f / amax : 0.f;
-#pragma unroll
-    for (int si = 0; si < NS; ++si) {
-      const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
-      int q1[8], q2[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
-        const float t0 = f.x * inv, t1 = f.y * inv;
-        const int a0 = max(-127, min(127, __float2int_rn(t0)));
-        const int a1 = max(-127, min(127, __float2int_rn(t1)));
-        q1[2 * e] = a0;
-        q1[2 * e + 1] = a1;
-        q2[2 * e] = max(-127, min(127, __float2int_rn((t0 - (float)a0) * 254.f)));
-        q2[2 * e + 1] = max(-127, min(127, __float2int_rn((t1 - (float)a1) * 254.f)));
-      }
-      dst[si] = make_uint4(pack_s8x4(q1[0], q1[1], q1[2], q1[3]),
-                           pack_s8x4(q1[4], q1[5], q1[6], q1[7]),
-                           pack_s8x4(q2[0], q2[1], q2[2], q2[3]),
-                           pack_s8x4(q2[4], q2[5], q2[6], q2[7]));
-    }
-  };
-
   auto convert_q = [&]() {
-    if constexpr (I8) {
-      split_row(ra, qa, qsc0);
-      if constexpr (GT == 16) {
-        split_row(rb, qb, qsc1);
-      } else {
 #pragma unroll
-        for (int si = 0; si < NS; ++si) qb[si] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    } else {
-#pragma unroll
-      for (int si = 0; si < NS; ++si) {
-        qa[si] = ra[si];
-        qb[si] = rb[si];
-      }
+    for (int si = 0; si < NS; ++si) {
+      qa[si] = ra[si];
+      qb[si] = rb[si];
     }
   };
   // The first piece's q rows are requested before the page copies, so their latency overlaps
@@ -819,8 +782,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   // ---- 4. Producer: the copies of 32 upcoming pages, one per lane, as (row << 3) | subpage,
   // where row = block * kv_heads + kv_head indexes [num_blocks * kv_heads] page rows.
-  auto batch_info = [&](int jbase) {
+  // With a decode step, wr receives the sequence whose new token lies in the page (the last
+  // page of a segment whose context and block id are valid), else -1.
+  const bool step_write = a.new_k != nullptr;
+  auto batch_info = [&](int jbase, int& wr) {
     int pk = 0;
+    wr = -1;
     const int j = jbase + lane;
     if (j < n) {
       int b, seg, sp;
@@ -829,23 +796,58 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       const int bi = sp / a.subs;
       const int sub = sp - bi * a.subs;
       int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + bi);
+      bool ok = true;
       if (blk < 0 || blk >= a.NB) {
         flag_error(a.status, PA_ERR_BLOCK_ID);
         blk = 0;
+        ok = false;
       }
       pk = ((blk * a.KVH + kvh) << 3) | sub;
+      if (step_write && ok && sp == pages_of(b) - 1 && __ldg(a.context_lens + b) <= cap) wr = b;
     }
     return pk;
   };
-  int cur = batch_info(0);
+  int curw = -1, nxtw = -1;
+  int cur = batch_info(0, curw);
   int nxt = 0;  // block ids of pages 32..63: read once the first copies are on their way
+
+  // The new token of sequence b, kv head row % KVH, written into page row `row` at offset
+  // (context - 1) % block_size by the whole warp; each lane fences its stores against the
+  // async proxy, so the page copy issued next reads them.
+  auto write_new_token = [&](int b, int row) {
+    const int kvh = row % a.KVH;
+    const int off = (s_ctx[b] - 1) % a.bs;
+    const size_t so = (size_t)b * a.new_stride + (size_t)kvh * D;
+    constexpr int KIND = I8 ? kRowsI8 : (F8 ? kRowsFP8 : kRowsF16);
+    auto rows = [&](auto tag) {
+      using T = decltype(tag);
+      warp_write_row<T, KIND, D>(static_cast<const T*>(a.new_k) + so, lane, false, a.kc_w,
+                                 a.ks_w, (size_t)row, off, a.bs, a.new_kfix);
+      warp_write_row<T, KIND, D>(static_cast<const T*>(a.new_v) + so, lane, true, a.vc_w,
+                                 a.vs_w, (size_t)row, off, a.bs, a.new_vfix);
+    };
+    if (a.new_dtype == PA_DTYPE_BF16) {
+      rows(__nv_bfloat16());
+    } else if (a.new_dtype == PA_DTYPE_F32) {
+      rows(0.f);
+    } else {
+      rows(__half());
+    }
+    fence_proxy_async_global();
+    __syncwarp();
+  };
 
   auto issue = [&](int j, int s) {
     if (j > 0 && (j & 31) == 0) {
       cur = nxt;
-      nxt = batch_info(j + 32);
+      curw = nxtw;
+      nxt = batch_info(j + 32, nxtw);
     }
     const int pk = __shfl_sync(0xffffffffu, cur, j & 31);
+    if (step_write) {
+      const int wb = __shfl_sync(0xffffffffu, curw, j & 31);
+      if (wb >= 0) write_new_token(wb, pk >> 3);
+    }
     if (lane == 0) {
       const int row = pk >> 3;
       const int sub = pk & 7;
@@ -881,7 +883,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __syncwarp();
   for (int j = 0; j < npro; ++j) issue(j, j);
   int issued = npro;
-  nxt = batch_info(32);
+  nxt = batch_info(32, nxtw);
   convert_q();
 
   // Shared-memory offsets of the K cells this lane reads (chunk of load si, token of n-tile
@@ -989,47 +991,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n); tokens 4r..4r+3 of
       // head g end up in x[0..3] (and of head g+8 in y[0..3]).
       float x[4], y[4];
-      if constexpr (I8) {
-        int sa[2][4], sbq[2][4];
-#pragma unroll
-        for (int jt = 0; jt < 2; ++jt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            sa[jt][e] = 0;
-            sbq[jt][e] = 0;
-          }
-#pragma unroll
-        for (int si = 0; si < NS; ++si) {
-#pragma unroll
-          for (int jt = 0; jt < 2; ++jt) {
-            imma_16832(sa[jt], qa[si].x, qb[si].x, qa[si].y, qb[si].y, k8[si][jt].x,
-                       k8[si][jt].y);
-            imma_16832(sbq[jt], qa[si].z, qb[si].z, qa[si].w, qb[si].w, k8[si][jt].x,
-                       k8[si][jt].y);
-          }
-        }
-        constexpr float kLo = 1.f / 254.f;
-        x[0] = fmaf((float)sbq[0][0], kLo, (float)sa[0][0]) * qsc0;
-        x[1] = fmaf((float)sbq[0][1], kLo, (float)sa[0][1]) * qsc0;
-        x[2] = fmaf((float)sbq[1][0], kLo, (float)sa[1][0]) * qsc0;
-        x[3] = fmaf((float)sbq[1][1], kLo, (float)sa[1][1]) * qsc0;
-        if constexpr (NT == 2) {
-          y[0] = fmaf((float)sbq[0][2], kLo, (float)sa[0][2]) * qsc1;
-          y[1] = fmaf((float)sbq[0][3], kLo, (float)sa[0][3]) * qsc1;
-          y[2] = fmaf((float)sbq[1][2], kLo, (float)sa[1][2]) * qsc1;
-          y[3] = fmaf((float)sbq[1][3], kLo, (float)sa[1][3]) * qsc1;
-        } else {
-          y[0] = y[1] = y[2] = y[3] = 0.f;
-        }
-      } else {
-        if constexpr (F8) {
-          // e4m3 K bytes -> exact fp16 (every e4m3 value is an fp16 value).
+      {
+        if constexpr (BYTE) {
+          // int8 (magic-exponent unpack) or e4m3 K bytes -> exact fp16.
 #pragma unroll
           for (int si = 0; si < NS; ++si)
 #pragma unroll
             for (int jt = 0; jt < 2; ++jt) {
-              e4m3x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
-              e4m3x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
+              if constexpr (I8) {
+                i8x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
+                i8x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
+              } else {
+                e4m3x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
+                e4m3x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
+              }
             }
         }
         // Two accumulation chains per n-tile (even / odd si) shorten the MMA dependency.
@@ -1121,14 +1096,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           }
         }
       }
+      // Weights are formed 2^kPExp times larger than p (the exponent is shifted), so that the
+      // fp16 hi/lo split of P' below stays clear of the fp16 subnormal range while P' (at most
+      // 2^kPExp times a V scale) stays below the fp16 maximum. O and l carry the same factor:
+      // it cancels in O / l and is taken out when a partial slot is written.
+      const float mb0 = m0 - kPExp;
+      const float mb1 = m1 - kPExp;
       float p[4], pv[4], py[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        p[e] = ex2(x[e] - m0);
+        p[e] = ex2(x[e] - mb0);
         l0 += p[e];
         pv[e] = p[e];
         if constexpr (NT == 2) {
-          py[e] = ex2(y[e] - m1);
+          py[e] = ex2(y[e] - mb1);
           l1 += py[e];
         } else {
           py[e] = 0.f;
@@ -1152,10 +1133,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           }
         }
       }
-      const uint32_t pb0 = pack_f16x2(pv[0], pv[1]);
-      const uint32_t pb1 = pack_f16x2(pv[2], pv[3]);
-      const uint32_t pc0 = pack_f16x2(py[0], py[1]);
-      const uint32_t pc1 = pack_f16x2(py[2], py[3]);
+      // P' as two fp16 parts, hi + lo (about 22 significant bits), each multiplied by V: one
+      // fp16 rounding of the weights alone can exceed the output tolerance when attention is
+      // concentrated on a few tokens with large V entries.
+      uint32_t pb0, pb1, pl0, pl1, pc0 = 0u, pc1 = 0u, pm0 = 0u, pm1 = 0u;
+      split_f16x2(pv[0], pv[1], pb0, pl0);
+      split_f16x2(pv[2], pv[3], pb1, pl1);
+      if constexpr (NT == 2) {
+        split_f16x2(py[0], py[1], pc0, pm0);
+        split_f16x2(py[2], py[3], pc1, pm1);
+      }
 
       // O^T += V^T P^T : rows = head_dim (16 per m-tile), columns = heads.
       uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
@@ -1184,7 +1171,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           a3 = v16[i][1].y & mhi;
         }
         mma_16816(oacc[i][0], a0, a1, a2, a3, pb0, pb1);
-        if constexpr (NT == 2) mma_16816(oacc[i][1], a0, a1, a2, a3, pc0, pc1);
+        mma_16816(oacc[i][0], a0, a1, a2, a3, pl0, pl1);
+        if constexpr (NT == 2) {
+          mma_16816(oacc[i][1], a0, a1, a2, a3, pc0, pc1);
+          mma_16816(oacc[i][1], a0, a1, a2, a3, pm0, pm1);
+        }
       }
     }
 
@@ -1212,23 +1203,25 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       const int hbase = kvh * a.G + ht * GT;
       const int hcnt = min(GT, a.G - ht * GT);
 
+      // Partial slots hold O and l without the 2^kPExp weight factor (an exact rescale).
       auto write_slot = [&](float* slot) {
+        constexpr float kUnscale = 1.f / (float)(1 << (int)kPExp);
 #pragma unroll
         for (int i = 0; i < MT; ++i) {
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             *reinterpret_cast<float2*>(slot + (16 * i + g) * GT + nt * 8 + 2 * r) =
-                make_float2(oacc[i][nt][0], oacc[i][nt][1]);
+                make_float2(oacc[i][nt][0] * kUnscale, oacc[i][nt][1] * kUnscale);
             *reinterpret_cast<float2*>(slot + (16 * i + g + 8) * GT + nt * 8 + 2 * r) =
-                make_float2(oacc[i][nt][2], oacc[i][nt][3]);
+                make_float2(oacc[i][nt][2] * kUnscale, oacc[i][nt][3] * kUnscale);
           }
         }
         if (r == 0) {
           slot[D * GT + g] = m0;
-          slot[D * GT + GT + g] = lt0;
+          slot[D * GT + GT + g] = lt0 * kUnscale;
           if constexpr (NT == 2) {
             slot[D * GT + 8 + g] = m1;
-            slot[D * GT + GT + 8 + g] = lt1;
+            slot[D * GT + GT + 8 + g] = lt1 * kUnscale;
           }
         }
       };

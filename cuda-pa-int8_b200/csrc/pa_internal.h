@@ -45,6 +45,20 @@ struct DecodeArgs {
   int total_warps;
   int bulk;                    // 1: V and scales via 1-D bulk copies (block_size == 16)
   float qk_scale_log2;         // scale * log2(e)
+  // Decode step (new_k non-null): every sequence's new token, at position context_lens[b] - 1,
+  // is written into the cache by the warp that reads the page holding it, right before that
+  // page's copy is issued (only when one head tile covers each kv head, so that exactly one
+  // warp reads the page).
+  const void* new_k;           // [B, KVH, D] rows in new_dtype, new_stride elements per token
+  const void* new_v;
+  int new_dtype;               // PA_DTYPE_F16, PA_DTYPE_BF16 or PA_DTYPE_F32
+  long long new_stride;
+  const float* new_kfix;       // int8 per-tensor scales (null: per-token)
+  const float* new_vfix;
+  void* kc_w;                  // cache and scale bases the write stores into
+  void* vc_w;
+  float* ks_w;
+  float* vs_w;
 };
 
 struct ReduceArgs {
@@ -74,6 +88,13 @@ cudaError_t launch_write_rows(int in_dtype, int kind, int D, const void* k, cons
                               void* kc, void* vc, float* ks, float* vs, int NB, int bs,
                               const float* kfix, const float* vfix, int* status,
                               cudaStream_t st);
+// The decode step's new-token write as its own kernel (one warp per sequence x kv head x K|V;
+// slot from block_table and context_lens), for shapes where the fused write does not apply.
+cudaError_t launch_step_rows(int in_dtype, int kind, const void* k, const void* v,
+                             long long token_stride, const int* block_table,
+                             const int* context_lens, int max_blocks, int B, int KVH, void* kc,
+                             void* vc, float* ks, float* vs, int NB, int bs, const float* kfix,
+                             const float* vfix, int* status, cudaStream_t st);
 cudaError_t launch_prefill(int in_dtype, bool i8, const void* k, const void* v, int S, int L,
                            int KVH, const int* bt, const int* cl, int max_blocks, void* kc,
                            void* vc, float* ks, float* vs, int NB, int bs, const float* kfix,

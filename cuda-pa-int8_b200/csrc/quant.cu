@@ -1,77 +1,27 @@
 // Cache-write kernels for B200: per-token symmetric INT8 quantize-into-cache, FP16
 // copy-into-cache, block-granular prefill scatter, and the per-tensor absmax scale.
 //
-// Quantisation is bit-exact with the reference quantizer quantize_per_token
-// (tests/paged_decode_attn.py:106-112):
-//   amax  = max_d |x_d|                     (exact in the input dtype)
-//   amax' = max(amax, T(1e-8))              (T = input dtype; T(1e-8) is 0 for fp16)
-//   scale = float(T(float(amax') / 127))    (IEEE fp32 divide, round-to-nearest-even into T)
-//   q_d   = clamp(rint(float(x_d) / scale), -127, 127)   (IEEE divide, half-to-even)
-// A zero scale (all-zero or tiny fp16 rows) gives x/0 = +-inf -> +-127 and 0/0 = NaN -> 0,
-// which is what the reference produces on the CPU. These kernels are built without fast-math
-// so the divides stay IEEE (__fdiv_rn is used explicitly as well).
+// The per-row quantisation (bit-exact with the reference's quantize_per_token,
+// tests/paged_decode_attn.py:106-112) lives in pa_rows.cuh, shared with the decode step's fused
+// new-token write. These kernels are built without fast-math so the divides stay IEEE.
 
 #include "pa_common.cuh"
 #include "pa_internal.h"
+#include "pa_rows.cuh"
 
 namespace pa {
 namespace {
 
-template <typename T> struct In;
-template <> struct In<__half> {
-  static __device__ __forceinline__ float ld(const __half* p) { return __half2float(*p); }
-  static __device__ __forceinline__ float clamp_floor() { return 0.f; }  // half(1e-8) == 0
-  static __device__ __forceinline__ float round_t(float v) {
-    return __half2float(__float2half_rn(v));
-  }
-};
-template <> struct In<__nv_bfloat16> {
-  static __device__ __forceinline__ float ld(const __nv_bfloat16* p) {
-    return __bfloat162float(*p);
-  }
-  static __device__ __forceinline__ float clamp_floor() {
-    return __bfloat162float(__float2bfloat16_rn(1e-8f));
-  }
-  static __device__ __forceinline__ float round_t(float v) {
-    return __bfloat162float(__float2bfloat16_rn(v));
-  }
-};
-template <> struct In<float> {
-  static __device__ __forceinline__ float ld(const float* p) { return *p; }
-  static __device__ __forceinline__ float clamp_floor() { return 1e-8f; }
-  static __device__ __forceinline__ float round_t(float v) { return v; }
-};
-
-// Per-token scale from the row absmax (quantize_per_token, tests/paged_decode_attn.py:109-110).
-template <typename T>
-__device__ __forceinline__ float token_scale(float amax) {
-  return In<T>::round_t(__fdiv_rn(fmaxf(amax, In<T>::clamp_floor()), 127.f));
-}
-
-__device__ __forceinline__ int8_t quant1(float x, float s) {
-  int q = __float2int_rn(__fdiv_rn(x, s));
-  q = q < -127 ? -127 : (q > 127 ? 127 : q);
-  return (int8_t)q;
-}
-
-// Load DPL consecutive input values starting at src (src aligned to DPL elements).
-template <typename T, int DPL>
-__device__ __forceinline__ void load_vals(const T* src, float (&x)[DPL]) {
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) x[e] = In<T>::ld(src + e);
-}
-
 // ---------------------------------------------------------------------------------------
 // Token-granular write: one warp per (token, kv-head, K|V) row.
 // ---------------------------------------------------------------------------------------
-template <typename T, bool I8, int D>
+template <typename T, int KIND, int D>
 __global__ void __launch_bounds__(256) write_rows_kernel(
     const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
     const int* __restrict__ slot_mapping, int N, int KVH, void* __restrict__ k_cache,
     void* __restrict__ v_cache, float* __restrict__ k_scales, float* __restrict__ v_scales,
     int NB, int bs, const float* __restrict__ kfix, const float* __restrict__ vfix,
     int* status) {
-  constexpr int DPL = D / 32;
   const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= (long long)N * KVH * 2) return;
@@ -87,64 +37,42 @@ __global__ void __launch_bounds__(256) write_rows_kernel(
     if (lane == 0) flag_error(status, PA_ERR_SLOT);
     return;
   }
-  const T* src = (which ? v : k) + (size_t)n * token_stride + (size_t)kvh * D + lane * DPL;
-  float x[DPL];
-  load_vals<T, DPL>(src, x);
-  const size_t page = (size_t)blk * KVH + kvh;
-  const int d0 = lane * DPL;
+  const T* src = (which ? v : k) + (size_t)n * token_stride + (size_t)kvh * D;
+  warp_write_row<T, KIND, D>(src, lane, which != 0, which ? v_cache : k_cache,
+                             which ? v_scales : k_scales, (size_t)blk * KVH + kvh, off, bs,
+                             which ? vfix : kfix);
+}
 
-  if constexpr (I8) {
-    float s;
-    const float* fix = which ? vfix : kfix;
-    if (fix != nullptr) {
-      s = __ldg(fix);
-    } else {
-      float am = 0.f;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) am = fmaxf(am, fabsf(x[e]));
-      am = warp_max(am);
-      s = token_scale<T>(am);
-    }
-    int8_t qv[DPL];
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) qv[e] = quant1(x[e], s);
-    int8_t* kc = reinterpret_cast<int8_t*>(k_cache);
-    int8_t* vc = reinterpret_cast<int8_t*>(v_cache);
-    if (which == 0) {
-      // K [.., D/8, bs, 8]: DPL (<= 8) consecutive d inside one 8-wide chunk.
-      int8_t* dst = kc + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
-      if constexpr (DPL == 4) {
-        *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(qv);
-      } else {
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) dst[e] = qv[e];
-      }
-      if (lane == 0) k_scales[page * bs + off] = s;
-    } else {
-      // V [.., D, bs]: one byte per head_dim row.
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) vc[(page * D + d0 + e) * bs + off] = qv[e];
-      if (lane == 0) v_scales[page * bs + off] = s;
-    }
-  } else {
-    __half hv[DPL];
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) hv[e] = __float2half_rn(x[e]);
-    __half* kc = reinterpret_cast<__half*>(k_cache);
-    __half* vc = reinterpret_cast<__half*>(v_cache);
-    if (which == 0) {
-      __half* dst = kc + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
-      if constexpr (DPL == 4) {
-        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(hv);
-      } else {
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) dst[e] = hv[e];
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) vc[(page * D + d0 + e) * bs + off] = hv[e];
-    }
+// ---------------------------------------------------------------------------------------
+// The decode step's new-token write: one warp per (sequence, kv-head, K|V) row; the token goes
+// to position context_lens[b] - 1 of sequence b, through its block table.
+// ---------------------------------------------------------------------------------------
+template <typename T, int KIND, int D>
+__global__ void __launch_bounds__(256) step_rows_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
+    const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
+    int B, int KVH, void* __restrict__ k_cache, void* __restrict__ v_cache,
+    float* __restrict__ k_scales, float* __restrict__ v_scales, int NB, int bs,
+    const float* __restrict__ kfix, const float* __restrict__ vfix, int* status) {
+  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long long)B * KVH * 2) return;
+  const int which = (int)(gw & 1);  // 0: K, 1: V
+  const long long row = gw >> 1;
+  const int b = (int)(row / KVH);
+  const int kvh = (int)(row - (long long)b * KVH);
+  const int ctx = __ldg(context_lens + b);
+  if (ctx < 1 || ctx > max_blocks * bs) return;  // the decode flags the length
+  const int pos = ctx - 1;
+  const int blk = __ldg(block_table + (size_t)b * max_blocks + pos / bs);
+  if (blk < 0 || blk >= NB) {
+    if (lane == 0) flag_error(status, PA_ERR_BLOCK_ID);
+    return;
   }
+  const T* src = (which ? v : k) + (size_t)b * token_stride + (size_t)kvh * D;
+  warp_write_row<T, KIND, D>(src, lane, which != 0, which ? v_cache : k_cache,
+                             which ? v_scales : k_scales, (size_t)blk * KVH + kvh, pos % bs, bs,
+                             which ? vfix : kfix);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -288,65 +216,6 @@ __global__ void scale_finalize_kernel(const unsigned int* amax_bits, float* scal
   *scale_out = s;
 }
 
-// Token-granular FP8 (e4m3) write, one warp per (token, kv-head, K|V) row: scale =
-// amax / 448 (IEEE fp32 divide), q = e4m3(x / scale) with round-to-nearest-even and saturation
-// to +-448; a zero row stores scale 0 and zeros. Same page layout as the INT8 cache.
-template <typename T, int D>
-__global__ void __launch_bounds__(256) write_rows_fp8_kernel(
-    const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
-    const int* __restrict__ slot_mapping, int N, int KVH, uint8_t* __restrict__ k_cache,
-    uint8_t* __restrict__ v_cache, float* __restrict__ k_scales, float* __restrict__ v_scales,
-    int NB, int bs, int* status) {
-  constexpr int DPL = D / 32;
-  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= (long long)N * KVH * 2) return;
-  const int which = (int)(gw & 1);  // 0: K, 1: V
-  const long long row = gw >> 1;
-  const int n = (int)(row / KVH);
-  const int kvh = (int)(row - (long long)n * KVH);
-  const int slot = __ldg(slot_mapping + n);
-  if (slot < 0) return;  // padding token
-  const int blk = slot / bs;
-  const int off = slot - blk * bs;
-  if (blk >= NB) {
-    if (lane == 0) flag_error(status, PA_ERR_SLOT);
-    return;
-  }
-  const T* src = (which ? v : k) + (size_t)n * token_stride + (size_t)kvh * D + lane * DPL;
-  float x[DPL];
-  load_vals<T, DPL>(src, x);
-  float am = 0.f;
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) am = fmaxf(am, fabsf(x[e]));
-  am = warp_max(am);
-  const float s = __fdiv_rn(am, 448.f);
-  uint8_t qv[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e)
-    qv[e] = s > 0.f ? (uint8_t)__nv_cvt_float_to_fp8(__fdiv_rn(x[e], s), __NV_SATFINITE,
-                                                     __NV_E4M3)
-                    : (uint8_t)0;
-  const size_t page = (size_t)blk * KVH + kvh;
-  const int d0 = lane * DPL;
-  if (which == 0) {
-    // K [.., D/8, bs, 8]: DPL (<= 8) consecutive d inside one 8-wide chunk.
-    uint8_t* dst = k_cache + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
-    if constexpr (DPL == 4) {
-      *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(qv);
-    } else {
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) dst[e] = qv[e];
-    }
-    if (lane == 0) k_scales[page * bs + off] = s;
-  } else {
-    // V [.., D, bs]: one byte per head_dim row.
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) v_cache[(page * D + d0 + e) * bs + off] = qv[e];
-    if (lane == 0) v_scales[page * bs + off] = s;
-  }
-}
-
 template <typename T>
 cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long long ts,
                           const int* slots, int N, int KVH, void* kc, void* vc, float* ks,
@@ -359,15 +228,38 @@ cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long lo
   const T* vv = static_cast<const T*>(v);
   if (D != 128) return cudaErrorInvalidValue;
   if (kind == kRowsFP8) {
-    write_rows_fp8_kernel<T, 128><<<grid, 256, 0, st>>>(
-        kk, vv, ts, slots, N, KVH, static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), ks, vs,
-        NB, bs, status);
+    write_rows_kernel<T, kRowsFP8, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
+                                                              ks, vs, NB, bs, nullptr, nullptr,
+                                                              status);
   } else if (kind == kRowsI8) {
-    write_rows_kernel<T, true, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc, ks,
-                                                          vs, NB, bs, kf, vf, status);
+    write_rows_kernel<T, kRowsI8, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
+                                                             ks, vs, NB, bs, kf, vf, status);
   } else {
-    write_rows_kernel<T, false, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
-                                                           ks, vs, NB, bs, kf, vf, status);
+    write_rows_kernel<T, kRowsF16, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
+                                                              ks, vs, NB, bs, kf, vf, status);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_step_rows_t(int kind, const void* k, const void* v, long long ts,
+                               const int* bt, const int* cl, int max_blocks, int B, int KVH,
+                               void* kc, void* vc, float* ks, float* vs, int NB, int bs,
+                               const float* kf, const float* vf, int* status, cudaStream_t st) {
+  const long long warps = (long long)B * KVH * 2;
+  const int grid = (int)((warps + 7) / 8);
+  if (grid == 0) return cudaSuccess;
+  const T* kk = static_cast<const T*>(k);
+  const T* vv = static_cast<const T*>(v);
+  if (kind == kRowsFP8) {
+    step_rows_kernel<T, kRowsFP8, 128><<<grid, 256, 0, st>>>(
+        kk, vv, ts, bt, cl, max_blocks, B, KVH, kc, vc, ks, vs, NB, bs, nullptr, nullptr, status);
+  } else if (kind == kRowsI8) {
+    step_rows_kernel<T, kRowsI8, 128><<<grid, 256, 0, st>>>(
+        kk, vv, ts, bt, cl, max_blocks, B, KVH, kc, vc, ks, vs, NB, bs, kf, vf, status);
+  } else {
+    step_rows_kernel<T, kRowsF16, 128><<<grid, 256, 0, st>>>(
+        kk, vv, ts, bt, cl, max_blocks, B, KVH, kc, vc, ks, vs, NB, bs, nullptr, nullptr, status);
   }
   return cudaGetLastError();
 }
@@ -410,6 +302,25 @@ cudaError_t launch_write_rows(int in_dtype, int kind, int D, const void* k, cons
     case PA_DTYPE_F32:
       return launch_rows_t<float>(kind, D, k, v, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf,
                                   vf, status, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_step_rows(int in_dtype, int kind, const void* k, const void* v,
+                             long long ts, const int* bt, const int* cl, int max_blocks, int B,
+                             int KVH, void* kc, void* vc, float* ks, float* vs, int NB, int bs,
+                             const float* kf, const float* vf, int* status, cudaStream_t st) {
+  switch (in_dtype) {
+    case PA_DTYPE_F16:
+      return launch_step_rows_t<__half>(kind, k, v, ts, bt, cl, max_blocks, B, KVH, kc, vc, ks,
+                                        vs, NB, bs, kf, vf, status, st);
+    case PA_DTYPE_BF16:
+      return launch_step_rows_t<__nv_bfloat16>(kind, k, v, ts, bt, cl, max_blocks, B, KVH, kc,
+                                               vc, ks, vs, NB, bs, kf, vf, status, st);
+    case PA_DTYPE_F32:
+      return launch_step_rows_t<float>(kind, k, v, ts, bt, cl, max_blocks, B, KVH, kc, vc, ks,
+                                       vs, NB, bs, kf, vf, status, st);
     default:
       return cudaErrorInvalidValue;
   }

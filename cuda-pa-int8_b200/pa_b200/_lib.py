@@ -68,6 +68,8 @@ SIGNATURES = {
                            _vp, _sz, _vp]),
     "pa_quantize_into_cache_fp8": (_i, [_vp, _vp, _i, _i64, _vp, _i, _i, _i, _vp, _vp, _vp, _vp,
                                         _i, _i, _vp, _vp]),
+    "pa_decode_step": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                            _vp, _i, _i, _i, _i, _i, _i, _i, _f, _i, _i, _vp, _sz, _vp]),
     "pa_partial_floats": (_i, [_i, _i, _i]),
     "pa_decode_partial": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                                _i, _i, _f, _vp, _sz, _vp]),

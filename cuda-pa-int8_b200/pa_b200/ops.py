@@ -235,6 +235,61 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
     return out
 
 
+def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_lens, scale,
+                block_size=16, *, k_scales=None, v_scales=None, k_scale=None, v_scale=None,
+                splitk=False, fused=True, validate=True):
+    """One decode step: append every sequence's new token to the cache, then decode.
+
+    context_lens already counts the new token: new_k / new_v [num_seqs, kv_heads, head_dim]
+    (fp16, bf16 or fp32 rows) go to position context_lens[b] - 1 of sequence b through
+    block_table, written like quantize_into_cache (int8 cache, per-token scales or the
+    per-tensor k_scale / v_scale), its FP8 counterpart or write_into_cache (fp16 cache); then
+    the decode of decode() runs over the whole context. This is the bridge's
+    PagedKVCache.decode_append + split-K op (benchmarks/int8_bridge/paged_cache.py:132-156,
+    qwen_paged_attn.py:61-73) for a whole batch in one call. With fused=True (and at most 16 q
+    heads per kv head) the decode kernel writes each token itself just before reading its
+    page, so a step is one launch (two with splitk); fused=False runs the write as its own
+    kernel first. Both give bit-identical caches and outputs.
+
+    With validate=False the call does no host synchronisation and allocates nothing once the
+    stream's workspace exists, so after one call on a stream it can be captured in a CUDA
+    graph (the kernels still flag bad lengths in the status word).
+    """
+    kind = _kv_kind(k_cache, k_scales)
+    B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
+                                          block_size, kind, k_scales, v_scales)
+    _check_rows(new_k, new_v)
+    _require(tuple(new_k.shape) == (B, KVH, D), "new_k/new_v must be [num_seqs, kv_heads, "
+             "head_dim]")
+    _require(new_k.device == q.device, "new_k/new_v must be on q's device")
+    if k_scale is not None or v_scale is not None:
+        _require(kind == "i8" and k_scale is not None and v_scale is not None,
+                 "per-tensor scales need an int8 cache and both of k_scale and v_scale")
+        for t in (k_scale, v_scale):
+            _require(t.dtype == torch.float32 and t.numel() == 1 and t.device == q.device,
+                     "fixed scales must be one fp32 element on q's device")
+    if B == 0:
+        return out
+    L = _lib.lib()
+    max_blocks = block_table.shape[1]
+    with _Guard(q.device):
+        kv = _KV_CODE[kind]
+        need = L.pa_decode_workspace_bytes(B, H, KVH, D, max_blocks, block_size, kv,
+                                           1 if splitk else 0)
+        _require(need > 0, "unsupported decode shape: " + _lib.last_error())
+        ws = workspace(q.device, need)
+        args = (kv, out.data_ptr(), q.data_ptr(), new_k.data_ptr(), new_v.data_ptr(),
+                _DTYPE_CODE[new_k.dtype], new_k.stride(0), k_cache.data_ptr(),
+                v_cache.data_ptr(), _ptr(k_scales), _ptr(v_scales), _ptr(k_scale),
+                _ptr(v_scale), block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D, NB,
+                block_size, max_blocks, float(scale), 1 if splitk else 0, 1 if fused else 0,
+                ws.data_ptr(), ws.numel(), _stream(q.device))
+        if validate:
+            _check_lengths(context_lens, max_blocks * block_size)
+        _lib.check(L.pa_decode_step(*args), "paged decode step")
+    return out
+
+
 def decode_bf16(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
                 k_scales=None, v_scales=None, splitk=False, validate=True):
     """decode() with bf16 activations: q and out are bf16, the cache fp16, per-token INT8 or

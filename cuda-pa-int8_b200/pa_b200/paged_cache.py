@@ -93,6 +93,28 @@ class PagedKVCache:
         self.lengths[layer_idx] = t + 1
         return t + 1
 
+    def append_and_decode(self, layer_idx, k, v, q, scale, out=None):
+        """decode_append(layer_idx, k, v) followed by the split-K decode of q [1, num_q_heads,
+        head_dim] over the layer's cache -- the bridge's decode step
+        (benchmarks/int8_bridge/qwen_paged_attn.py:61-73) -- as one fused call (the token is
+        written by the decode kernel). Returns out [1, num_q_heads, head_dim] fp16."""
+        t = self.lengths[layer_idx]
+        H, D = self.num_kv_heads, self.head_dim
+        q = q.contiguous()
+        out = torch.empty_like(q) if out is None else out
+        ctx = torch.tensor([t + 1], dtype=torch.int32, device=self.device)
+        kw = {}
+        if self.is_int8:
+            kw = dict(k_scales=self.k_scales[layer_idx], v_scales=self.v_scales[layer_idx])
+            if self.variant == "int8_per_tensor":
+                kw.update(k_scale=self._k_tensor_scale[layer_idx],
+                          v_scale=self._v_tensor_scale[layer_idx])
+        ops.decode_step(out, q, k.contiguous().view(1, H, D), v.contiguous().view(1, H, D),
+                        self.k_cache[layer_idx], self.v_cache[layer_idx], self.block_table, ctx,
+                        scale, self.block_size, splitk=True, validate=False, **kw)
+        self.lengths[layer_idx] = t + 1
+        return out
+
     # --- read path --------------------------------------------------------------------------
     def context_lens(self, layer_idx):
         return torch.tensor([self.lengths[layer_idx]], dtype=torch.int32, device=self.device)

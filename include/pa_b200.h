@@ -139,6 +139,30 @@ int pa_splitk_fp8(void* out, const void* q, const void* k_cache, const void* v_c
                   int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
                   float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Decode step: append every sequence's new token to the cache, then decode over the whole
+ * context, in one call. context_lens[b] already counts the new token; new_k / new_v
+ * [num_seqs, num_kv_heads, head_dim] (new_dtype F16, BF16 or F32, token stride
+ * new_token_stride elements) are written at position context_lens[b] - 1 of sequence b through
+ * block_table, quantised like pa_quantize_into_cache (int8; with k_fixed_scale / v_fixed_scale
+ * the per-tensor scales), like pa_quantize_into_cache_fp8 (fp8) or copied (fp16), and the
+ * decode (splitk: the split-K pair) reads them. With fused nonzero and at most 16 q heads per
+ * kv head, the decode kernel writes each token itself, in the warp that reads the token's
+ * page, just before that page's copy: no extra launch. Otherwise (fused zero, or larger
+ * groups) a write kernel runs first. Both give bit-identical caches and outputs.
+ * Replaces the reference bridge's decode step, PagedKVCache.decode_append
+ * (benchmarks/int8_bridge/paged_cache.py:132-156) followed by the split-K op
+ * (benchmarks/int8_bridge/qwen_paged_attn.py:61-73), for a whole batch.
+ * ---------------------------------------------------------------------------------- */
+int pa_decode_step(int kv_dtype, void* out, const void* q, const void* new_k,
+                   const void* new_v, int new_dtype, int64_t new_token_stride, void* k_cache,
+                   void* v_cache, float* k_scales, float* v_scales, const float* k_fixed_scale,
+                   const float* v_fixed_scale, const int32_t* block_table,
+                   const int32_t* context_lens, int num_seqs, int num_heads, int num_kv_heads,
+                   int head_dim, int num_blocks, int block_size, int max_blocks_per_seq,
+                   float scale, int splitk, int fused, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
 /* FP16 single-pass decode that allocates nothing and takes no workspace, for callers that
  * cannot allocate device memory when they run attention: plugins whose host framework owns
  * all device memory, and serving loops that must stay out of any allocator. Its scratch is a

@@ -85,7 +85,8 @@ def test_extension_entry_points_check_arguments_on_the_host(lib):
     for must in ("pa_decode_fp8", "pa_splitk_fp8", "pa_quantize_into_cache_fp8",
                  "pa_decode_bf16q", "pa_decode_bf16q_workspace_bytes",
                  "pa_selftest_bounded_wait", "pa_decode_f16_noalloc",
-                 "pa_decode_f16_noalloc_read_status", "pa_reset_workspace"):
+                 "pa_decode_f16_noalloc_read_status", "pa_reset_workspace",
+                 "pa_decode_step"):
         assert must in names
     assert b"fp16 range" in lib.pa_status_string(_lib.PA_ERR_Q_RANGE)
     p = 1 << 20
@@ -107,6 +108,19 @@ def test_extension_entry_points_check_arguments_on_the_host(lib):
     rc = lib.pa_quantize_into_cache_fp8(p, p, _lib.PA_DTYPE_F16, 256, p, 4, 2, 128, p, p, None, p,
                                         4, 16, None, None)
     assert rc == _lib.PA_ERR_INVALID_ARG
+    # decode step: cache dtype, new-token rows, per-tensor scales only with int8
+    rc = lib.pa_decode_step(_lib.PA_DTYPE_F32, p, p, p, p, _lib.PA_DTYPE_F16, 256, p, p, p, p,
+                            None, None, p, p, 1, 8, 2, 128, 4, 16, 2, 0.1, 0, 1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_UNSUPPORTED
+    rc = lib.pa_decode_step(_lib.PA_DTYPE_I8, p, p, None, p, _lib.PA_DTYPE_F16, 256, p, p, p, p,
+                            None, None, p, p, 1, 8, 2, 128, 4, 16, 2, 0.1, 0, 1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_INVALID_ARG
+    rc = lib.pa_decode_step(_lib.PA_DTYPE_F16, p, p, p, p, _lib.PA_DTYPE_F16, 256, p, p, None,
+                            None, p, p, p, p, 1, 8, 2, 128, 4, 16, 2, 0.1, 0, 1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_INVALID_ARG and b"fixed scales" in lib.pa_last_error()
+    rc = lib.pa_decode_step(_lib.PA_DTYPE_I8, p, p, p, p, _lib.PA_DTYPE_F16, 100, p, p, p, p,
+                            None, None, p, p, 1, 8, 2, 128, 4, 16, 2, 0.1, 0, 1, p, 1 << 30, None)
+    assert rc == _lib.PA_ERR_INVALID_ARG and b"new_token_stride" in lib.pa_last_error()
     # the wait self-test needs a status word; reset and status reads need their buffers
     assert lib.pa_selftest_bounded_wait(None, None) == _lib.PA_ERR_INVALID_ARG
     assert lib.pa_reset_workspace(None, 1024, None) == _lib.PA_ERR_INVALID_ARG
