@@ -25,7 +25,8 @@ and, at one GPU, the cache-write kernels alone ("write_kernels": 512 B read + 26
 (token, kv head)). Every config carries a parity check of its timed output against an fp32
 restatement of the reference decode in torch on the device (2e-3 abs + 1e-2 rel), its
 roofline and, at one GPU, a CPU baseline. Configs 3/3_f16/3_pt/6 and the write kernels run at
-one GPU only. --config NAME measures only that workload (as the headline).
+one GPU only. --config NAME measures only that workload (as the headline); --config writes
+only the cache-write kernels.
 
 Inputs are synthetic (seeded), larger than L2 (126 MB); timing is CUDA events on the launching
 stream around one replay of a CUDA graph of K steps, max over ranks.
@@ -100,7 +101,8 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", default=None,
-                   help="measure only this workload (2..6 or a name from SPECS)")
+                   help="measure only this workload (2..6, a name from SPECS, or 'writes' "
+                        "for the cache-write kernels alone)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--splitk", action="store_true", help="use the split-K pair")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -108,7 +110,7 @@ def parse():
     p.add_argument("--soak-ms", type=float, default=1500.0,
                    help="untimed load before the timed region so the clock sampler sees it")
     a = p.parse_args()
-    if a.config is not None:
+    if a.config is not None and a.config != "writes":
         a.config = config_name(a.config)
         if a.config not in SPECS:
             p.error(f"unknown config {a.config}")
@@ -815,46 +817,65 @@ def e2e_measure(torch, w, args, dist, device, total_bytes, total_seqs):
                           torch.empty_like(w.context_lens), torch.empty_like(w.out))
     scale = 1.0 / math.sqrt(HEAD_DIM)
 
+    split = args.splitk or w.splitk
+
     def e2e_step():
         dq.copy_(hq, non_blocking=True)
         dbt.copy_(hbt, non_blocking=True)
         dcl.copy_(hcl, non_blocking=True)
+        # The library's public ops, with the lengths checked on the pinned host copy they were
+        # uploaded from (the reference's context_lens >= 1 check, without a device sync).
         if w.step_tokens:
-            # A decode step: the library's step API (the reference has no batched step op).
             ops.decode_step(dout, dq, w.new_k, w.new_v, w.k_cache, w.v_cache, dbt, dcl, scale,
                             BLOCK, k_scales=w.k_scales, v_scales=w.v_scales, k_scale=w.k_fix,
-                            v_scale=w.v_fix, splitk=args.splitk or w.splitk)
-        elif w.kv == "f8":
-            # No reference op takes an FP8 cache: the library's own decode op.
-            ops.decode(dout, dq, w.k_cache, w.v_cache, dbt, dcl, scale, BLOCK,
-                       k_scales=w.k_scales, v_scales=w.v_scales, splitk=args.splitk)
-        elif w.kv == "i8":
-            name = "splitk_int8" if (args.splitk or w.splitk) else "warp_int8"
-            cuda_ext.VARIANTS_INT8[name](dout, dq, w.k_cache, w.v_cache, w.k_scales,
-                                         w.v_scales, dbt, dcl, scale, BLOCK)
+                            v_scale=w.v_fix, splitk=split, host_context_lens=hcl)
         else:
-            name = "splitk" if args.splitk else "warp"
-            cuda_ext.VARIANTS[name](dout, dq, w.k_cache, w.v_cache, dbt, dcl, scale, BLOCK)
+            ops.decode(dout, dq, w.k_cache, w.v_cache, dbt, dcl, scale, BLOCK,
+                       k_scales=w.k_scales, v_scales=w.v_scales, splitk=split,
+                       host_context_lens=hcl)
         hout.copy_(dout, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
-    for _ in range(3):
-        e2e_step()
-    if dist:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        e2e_step()
-    e2e_s = (time.perf_counter() - t0) / args.steps
-    e2e_s = _max_over_ranks(torch, dist, device, [e2e_s])[0]
+    def e2e_step_reference_names():
+        """The same step through the reference's op names (cuda_ext), whose context_lens
+        check reads the device tensor back (one synchronisation per call)."""
+        dq.copy_(hq, non_blocking=True)
+        dbt.copy_(hbt, non_blocking=True)
+        dcl.copy_(hcl, non_blocking=True)
+        if w.kv == "i8":
+            cuda_ext.VARIANTS_INT8["splitk_int8" if split else "warp_int8"](
+                dout, dq, w.k_cache, w.v_cache, w.k_scales, w.v_scales, dbt, dcl, scale, BLOCK)
+        else:
+            cuda_ext.VARIANTS["splitk" if split else "warp"](dout, dq, w.k_cache, w.v_cache,
+                                                             dbt, dcl, scale, BLOCK)
+        hout.copy_(dout, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        return _max_over_ranks(torch, dist, device, [(time.perf_counter() - t0) / args.steps])[0]
+
+    e2e_s = timed(e2e_step)
     h2d = (hq.numel() * hq.element_size() + hbt.numel() * 4 + hcl.numel() * 4)
     d2h = hout.numel() * hout.element_size()
-    return {"value": total_bytes / e2e_s / 1e9, "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "seqs_per_s": total_seqs / e2e_s, "ms_per_step": e2e_s * 1e3,
-            "path": ("pa_b200.ops.decode_step" if w.step_tokens else
-                     "pa_b200.ops.decode" if w.kv == "f8" else "pa_b200.cuda_ext") +
-                    " (validate=True: one context_lens host check/step)"}
+    rec = {"value": total_bytes / e2e_s / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "seqs_per_s": total_seqs / e2e_s, "ms_per_step": e2e_s * 1e3,
+           "path": ("pa_b200.ops.decode_step" if w.step_tokens else "pa_b200.ops.decode") +
+                   " with host_context_lens (lengths checked on the pinned host copy)"}
+    if not w.step_tokens and w.kv != "f8":
+        ref_s = timed(e2e_step_reference_names)
+        rec["reference_names"] = {"value": total_bytes / ref_s / 1e9, "unit": "GB/s",
+                                  "ms_per_step": ref_s * 1e3,
+                                  "path": "pa_b200.cuda_ext (reference op names: one "
+                                          "context_lens device read-back per call)"}
+    return rec
 
 
 def main():
@@ -891,6 +912,17 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=device)
     peak, peak_kind = measured_peak()
+
+    if args.config == "writes":
+        # The cache-write kernels alone (one GPU), as recorded under configs.write_kernels.
+        rec = write_kernels(torch, device, peak, args.steps)
+        if rank == 0:
+            print(json.dumps({"metric": "cache-write achieved HBM GB/s", "unit": "GB/s",
+                              "n_gpus": 1, "steps": args.steps, "write_kernels": rec}),
+                  flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return 0
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:

@@ -320,9 +320,11 @@ int decode_impl(int mode, int kv_i8, void* out, float* part_out, const void* q,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   // A decode step writes its new tokens first: inside the decode kernel when exactly one warp
-  // reads each page (one head tile per kv head), else as its own launch before the decode.
+  // reads each page (one head tile per kv head) and the rows can be bulk-copied (16-bit rows,
+  // 16-byte aligned), else as its own launch before the decode.
   const int row_kind = kv_i8 == 1 ? pa::kRowsI8 : (kv_i8 == 2 ? pa::kRowsFP8 : pa::kRowsF16);
-  const bool fuse = sw != nullptr && sw->fused && s.HT == 1;
+  const bool fuse = sw != nullptr && sw->fused && s.HT == 1 && sw->dtype != PA_DTYPE_F32 &&
+                    aligned(sw->k, 16) && aligned(sw->v, 16) && (sw->stride * 2) % 16 == 0;
   if (sw != nullptr && !fuse) {
     cudaError_t e = pa::launch_step_rows(
         sw->dtype, row_kind, sw->k, sw->v, sw->stride, block_table, context_lens, max_blocks, B,

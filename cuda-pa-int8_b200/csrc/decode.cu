@@ -77,6 +77,10 @@ struct Tile {
   static constexpr int SLOT = (D + 2) * GT;         // partial slot floats
   static constexpr size_t SMEM = 1024 + (size_t)WARPS * DEPTH * (KT + VT + ST) +
                                  (size_t)WARPS * DEPTH * 8;
+  // Decode step launches: per stage, the new token's K and V rows (16-bit) when the stage's
+  // page holds a sequence's new token.
+  static constexpr int NR = 2 * D * 2;
+  static constexpr size_t SMEM_STEP = SMEM + 16 + (size_t)WARPS * DEPTH * NR;
 };
 
 // ---------------------------------------------------------------------------------------
@@ -85,8 +89,10 @@ struct Tile {
 // lane owning head_dim rows [lane*D/32, (lane+1)*D/32). Several of these run in parallel,
 // one per warp.
 // ---------------------------------------------------------------------------------------
-// Largest merge a single warp takes when its CTA owes many merges; larger ones go to the
-// four-warp groups, whose merges need fewer dependent round trips.
+// Largest merge a single warp takes; larger ones go to the four-warp groups, whose merges
+// need fewer dependent round trips. The routine is chosen from the piece count alone, so a
+// segment's summation order, and the output's bits, do not depend on which CTA happens to
+// finish the segment last.
 constexpr int kWarpMergeMax = 8;
 
 template <int D, int GT, int P, typename PieceFn>
@@ -580,6 +586,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ int s_empty;
   __shared__ int s_pend[WARPS][2][6];
   __shared__ int s_npend[WARPS];
+  __shared__ int s_wrow[WARPS][DEPTH];  // decode step: page row whose new token a stage holds
   extern __shared__ __align__(16) uint8_t dsm_raw[];
 
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
@@ -587,6 +594,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   uint8_t* v_tiles = k_tiles + WARPS * DEPTH * C::KT;
   uint8_t* s_tiles = v_tiles + WARPS * DEPTH * C::VT;
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_tiles + WARPS * DEPTH * C::ST);
+  // New-token rows of a decode step (allocated only for step launches).
+  uint8_t* r_tiles = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(bars + WARPS * DEPTH) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -811,32 +821,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   int cur = batch_info(0, curw);
   int nxt = 0;  // block ids of pages 32..63: read once the first copies are on their way
 
-  // The new token of sequence b, kv head row % KVH, written into page row `row` at offset
-  // (context - 1) % block_size by the whole warp; each lane fences its stores against the
-  // async proxy, so the page copy issued next reads them.
-  auto write_new_token = [&](int b, int row) {
-    const int kvh = row % a.KVH;
-    const int off = (s_ctx[b] - 1) % a.bs;
-    const size_t so = (size_t)b * a.new_stride + (size_t)kvh * D;
-    constexpr int KIND = I8 ? kRowsI8 : (F8 ? kRowsFP8 : kRowsF16);
-    auto rows = [&](auto tag) {
-      using T = decltype(tag);
-      warp_write_row<T, KIND, D>(static_cast<const T*>(a.new_k) + so, lane, false, a.kc_w,
-                                 a.ks_w, (size_t)row, off, a.bs, a.new_kfix);
-      warp_write_row<T, KIND, D>(static_cast<const T*>(a.new_v) + so, lane, true, a.vc_w,
-                                 a.vs_w, (size_t)row, off, a.bs, a.new_vfix);
-    };
-    if (a.new_dtype == PA_DTYPE_BF16) {
-      rows(__nv_bfloat16());
-    } else if (a.new_dtype == PA_DTYPE_F32) {
-      rows(0.f);
-    } else {
-      rows(__half());
-    }
-    fence_proxy_async_global();
-    __syncwarp();
-  };
-
   auto issue = [&](int j, int s) {
     if (j > 0 && (j & 31) == 0) {
       cur = nxt;
@@ -844,17 +828,26 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       nxt = batch_info(j + 32, nxtw);
     }
     const int pk = __shfl_sync(0xffffffffu, cur, j & 31);
-    if (step_write) {
-      const int wb = __shfl_sync(0xffffffffu, curw, j & 31);
-      if (wb >= 0) write_new_token(wb, pk >> 3);
-    }
+    // Decode step: the page holding sequence wb's new token also brings the token's K and V
+    // rows (bulk copies on the same barrier); the consumer quantises them into the stage.
+    const int wb = step_write ? __shfl_sync(0xffffffffu, curw, j & 31) : -1;
     if (lane == 0) {
       const int row = pk >> 3;
       const int sub = pk & 7;
       uint64_t* bar = &wbar[s];
       uint8_t* kd = k_tiles + (warp * DEPTH + s) * C::KT;
       uint8_t* vd = v_tiles + (warp * DEPTH + s) * C::VT;
-      mbar_arrive_expect_tx(bar, C::TX);
+      // Recorded before the arrival, whose release the consumer's wait acquires.
+      if (step_write) s_wrow[warp][s] = wb >= 0 ? row : -1;
+      mbar_arrive_expect_tx(bar, C::TX + (wb >= 0 ? (uint32_t)C::NR : 0u));
+      if (step_write) {
+        if (wb >= 0) {
+          const size_t so = ((size_t)wb * a.new_stride + (size_t)(row % a.KVH) * D) * 2;
+          uint8_t* rd = r_tiles + (warp * DEPTH + s) * C::NR;
+          bulk_g2s(rd, static_cast<const uint8_t*>(a.new_k) + so, D * 2, bar);
+          bulk_g2s(rd + D * 2, static_cast<const uint8_t*>(a.new_v) + so, D * 2, bar);
+        }
+      }
       if constexpr (BYTE) {
         tma_load_3d(kd, &tm_k, bar, sub * 128, 0, row);
       } else {
@@ -909,6 +902,54 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const uint32_t vbase = smem_u32(v_tiles) + warp * DEPTH * C::VT;
   const uint32_t sbase = BYTE ? smem_u32(s_tiles) + warp * DEPTH * C::ST : 0u;
 
+  // Decode step: the new token's rows in stage s (bulk-copied with the page) are quantised
+  // like the cache writes, placed into the staged page at token t of the subpage (the TMA
+  // brought the slot's previous contents), and stored into the cache at page row `row`,
+  // offset `off` for later steps. Only this warp reads the page, so nothing orders the
+  // global stores against the copies.
+  auto merge_new_token = [&](int st, int row, int t, int off) {
+    static_assert(D == 128, "one lane per four head_dim values");
+    constexpr int KIND = I8 ? kRowsI8 : (F8 ? kRowsFP8 : kRowsF16);
+    const uint8_t* rk = r_tiles + (warp * DEPTH + st) * C::NR;
+    RowQ<KIND, D> qk, qv;
+    if (a.new_dtype == PA_DTYPE_BF16) {
+      qk = warp_quantize_row<__nv_bfloat16, KIND, D>(
+          reinterpret_cast<const __nv_bfloat16*>(rk), lane, a.new_kfix);
+      qv = warp_quantize_row<__nv_bfloat16, KIND, D>(
+          reinterpret_cast<const __nv_bfloat16*>(rk + D * 2), lane, a.new_vfix);
+    } else {
+      qk = warp_quantize_row<__half, KIND, D>(reinterpret_cast<const __half*>(rk), lane,
+                                              a.new_kfix);
+      qv = warp_quantize_row<__half, KIND, D>(reinterpret_cast<const __half*>(rk + D * 2),
+                                              lane, a.new_vfix);
+    }
+    uint8_t* kt = k_tiles + (warp * DEPTH + st) * C::KT;
+    uint8_t* vt = v_tiles + (warp * DEPTH + st) * C::VT;
+    const int c = lane >> 1;  // the 8-wide head_dim chunk of this lane's four values
+    if constexpr (BYTE) {
+      const int o = c * 128 + ((((t >> 1) ^ (c & 7)) << 4) | ((t & 1) << 3)) + 4 * (lane & 1);
+      *reinterpret_cast<uint32_t*>(kt + o) = qk.w[0];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) vt[(4 * lane + e) * kSubTokens + t] = (uint8_t)row_elem(qv, e);
+      if (lane == 0) {
+        uint8_t* sd = s_tiles + (warp * DEPTH + st) * C::ST;
+        reinterpret_cast<float*>(sd)[t] = qk.s;
+        reinterpret_cast<float*>(sd + kVsOff)[t] = qv.s;
+      }
+    } else {
+      const int rr = 2 * c + (t >> 3);
+      const int o = rr * 128 + (((t & 7) ^ (rr & 7)) << 4) + 8 * (lane & 1);
+      *reinterpret_cast<uint2*>(kt + o) = make_uint2(qk.w[0], qk.w[1]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        reinterpret_cast<uint16_t*>(vt)[(4 * lane + e) * kSubTokens + t] =
+            (uint16_t)row_elem(qv, e);
+    }
+    store_row(qk, lane, false, a.kc_w, a.ks_w, (size_t)row, off, a.bs);
+    store_row(qv, lane, true, a.vc_w, a.vs_w, (size_t)row, off, a.bs);
+    __syncwarp();
+  };
+
   float m0 = neg_inf(), l0 = 0.f, m1 = neg_inf(), l1 = 0.f;
   float oacc[MT][NT][4];
 
@@ -949,6 +990,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
     // ---- stage -> registers, then hand the stage back to the TMA right away -------------------
     const int valid = min(kSubTokens, cctx - (csp + k) * kSubTokens);
+    if (step_write) {
+      const int wrow = s_wrow[warp][s];
+      if (wrow >= 0) merge_new_token(s, wrow, valid - 1, (cctx - 1) % a.bs);
+    }
     const uint32_t kb = kbase + s * C::KT;
     const uint32_t vb = vbase + s * C::VT;
     const uint32_t sb = sbase + s * C::ST;
@@ -1320,16 +1365,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   if (lane == 0) s_npend[warp] = npend;
   __syncthreads();  // every warp is past its page loop: the ring memory is free scratch
   float* scratch = reinterpret_cast<float*>(k_tiles);
-  // A CTA with many merges runs them one per warp in parallel; one with a few merges deals
-  // the larger of them to its groups of four warps. 16-row head tiles keep more registers per
-  // piece and never merge in a single warp.
-  int n_merges = 0;
-  for (int w = 0; w < WARPS; ++w) n_merges += s_npend[w];
+  // Merges of up to kWarpMergeMax pieces run one per warp in parallel, larger ones in the
+  // groups of four warps. 16-row head tiles keep more registers per piece and never merge in
+  // a single warp.
   // Pieces per step of a one-warp merge: four where the launch leaves 255 registers a thread
   // (8 warps), two under the 168 of 12-warp launches.
   constexpr int kWarpStep = (WARPS <= 8) ? 4 : 2;
-  const int kWarpMerge =
-      (GT != 8) ? 0 : (n_merges * 4 >= WARPS ? kWarpMergeMax : 4);
+  constexpr int kWarpMerge = (GT != 8) ? 0 : kWarpMergeMax;
   int idx = 0;
   for (int w = 0; w < WARPS; ++w) {
     for (int e = 0; e < s_npend[w]; ++e) {
@@ -1477,19 +1519,23 @@ cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
   constexpr int W = Shape<KVK, GT>::W;
   constexpr int DP = Shape<KVK, GT>::DP;
   using C = Tile<KVK, 128, GT, DP, W>;
+  static_assert(C::SMEM_STEP + 9 * 1024 <= 227 * 1024, "shared memory of a step launch");
   auto kern = decode_kernel<KVK, 128, GT, DP, W>;
-  // The shared-memory opt-in is a per-device function attribute: set it once per device.
+  // The shared-memory opt-in is a per-device function attribute: set it once per device, to
+  // the larger size of a decode step launch.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)C::SMEM_STEP);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  kern<<<grid, W * 32, C::SMEM, stream>>>(a, maps[0], maps[1], maps[2], maps[3]);
+  const size_t smem = a.new_k != nullptr ? C::SMEM_STEP : C::SMEM;
+  kern<<<grid, W * 32, smem, stream>>>(a, maps[0], maps[1], maps[2], maps[3]);
   return cudaGetLastError();
 }
 

@@ -46,12 +46,12 @@ struct DecodeArgs {
   int bulk;                    // 1: V and scales via 1-D bulk copies (block_size == 16)
   float qk_scale_log2;         // scale * log2(e)
   // Decode step (new_k non-null): every sequence's new token, at position context_lens[b] - 1,
-  // is written into the cache by the warp that reads the page holding it, right before that
-  // page's copy is issued (only when one head tile covers each kv head, so that exactly one
-  // warp reads the page).
-  const void* new_k;           // [B, KVH, D] rows in new_dtype, new_stride elements per token
-  const void* new_v;
-  int new_dtype;               // PA_DTYPE_F16, PA_DTYPE_BF16 or PA_DTYPE_F32
+  // is quantised by the warp that reads the page holding it (its rows arrive with the page's
+  // copy), placed into the staged page and stored into the cache (only when one head tile
+  // covers each kv head, so that exactly one warp reads the page).
+  const void* new_k;           // [B, KVH, D] 16-bit rows (16-byte aligned), new_stride elements
+  const void* new_v;           //   per token (a multiple of 8)
+  int new_dtype;               // PA_DTYPE_F16 or PA_DTYPE_BF16
   long long new_stride;
   const float* new_kfix;       // int8 per-tensor scales (null: per-token)
   const float* new_vfix;

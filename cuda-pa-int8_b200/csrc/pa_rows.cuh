@@ -62,41 +62,35 @@ __device__ __forceinline__ void load_vals(const T* src, float (&x)[DPL]) {
   for (int e = 0; e < DPL; ++e) x[e] = In<T>::ld(src + e);
 }
 
-// One warp writes one row (K or V) of one (token, kv head) into the paged cache: page row
-// `page` (= block * kv_heads + kv_head), token offset `off` inside the block. Lane l owns the
-// D/32 consecutive values starting at src + l * D/32. KIND: kRowsF16 (fp16 copy), kRowsI8
-// (per-token int8, or the fixed per-tensor scale *fix when fix is non-null), kRowsFP8
-// (per-token e4m3). Lane 0 writes the scale slot.
-//   K page [D/8][bs][8]: a lane's values lie inside one 8-wide chunk (one store);
-//   V page [D][bs]:      one element per head_dim row.
+// One row of one (token, kv head), quantised by one warp: lane l's D/32 consecutive values
+// (from src + l * D/32) packed in storage order -- DPL bytes (int8 or e4m3) or DPL fp16
+// halves -- and the row's scale. KIND: kRowsF16 (fp16 copy), kRowsI8 (per-token int8, or the
+// fixed per-tensor scale *fix when fix is non-null), kRowsFP8 (per-token e4m3).
+template <int KIND, int D>
+struct RowQ {
+  static constexpr int DPL = D / 32;
+  static constexpr int WORDS = KIND == kRowsF16 ? DPL / 2 : DPL / 4;
+  uint32_t w[WORDS];
+  float s;
+};
+
 template <typename T, int KIND, int D>
-__device__ __forceinline__ void warp_write_row(const T* src, int lane, bool is_v, void* cache,
-                                               float* scales, size_t page, int off, int bs,
-                                               const float* fix) {
+__device__ __forceinline__ RowQ<KIND, D> warp_quantize_row(const T* src, int lane,
+                                                           const float* fix) {
   constexpr int DPL = D / 32;
+  static_assert(DPL % 4 == 0, "a lane packs whole 32-bit words");
+  RowQ<KIND, D> r;
   float x[DPL];
   load_vals<T, DPL>(src + lane * DPL, x);
-  const int d0 = lane * DPL;
   if constexpr (KIND == kRowsF16) {
-    __half hv[DPL];
+    r.s = 0.f;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) hv[e] = __float2half_rn(x[e]);
-    __half* c = reinterpret_cast<__half*>(cache);
-    if (!is_v) {
-      __half* dst = c + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
-      if constexpr (DPL == 4) {
-        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(hv);
-      } else {
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) dst[e] = hv[e];
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) c[(page * D + d0 + e) * bs + off] = hv[e];
+    for (int e = 0; e < DPL; e += 2) {
+      const __half2 h = __floats2half2_rn(x[e], x[e + 1]);
+      r.w[e / 2] = *reinterpret_cast<const uint32_t*>(&h);
     }
   } else {
     float s;
-    uint8_t qv[DPL];
     if (KIND == kRowsI8 && fix != nullptr) {
       s = __ldg(fix);
     } else {
@@ -106,6 +100,7 @@ __device__ __forceinline__ void warp_write_row(const T* src, int lane, bool is_v
       am = warp_max(am);
       s = (KIND == kRowsI8) ? token_scale<T>(am) : __fdiv_rn(am, 448.f);
     }
+    uint8_t qv[DPL];
     if constexpr (KIND == kRowsI8) {
 #pragma unroll
       for (int e = 0; e < DPL; ++e) qv[e] = (uint8_t)quant1(x[e], s);
@@ -116,21 +111,75 @@ __device__ __forceinline__ void warp_write_row(const T* src, int lane, bool is_v
                                                          __NV_E4M3)
                         : (uint8_t)0;
     }
-    uint8_t* c = reinterpret_cast<uint8_t*>(cache);
-    if (!is_v) {
-      uint8_t* dst = c + (page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7);
-      if constexpr (DPL == 4) {
-        *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(qv);
-      } else {
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) dst[e] = qv[e];
-      }
+    for (int e = 0; e < DPL; e += 4)
+      r.w[e / 4] = (uint32_t)qv[e] | ((uint32_t)qv[e + 1] << 8) | ((uint32_t)qv[e + 2] << 16) |
+                   ((uint32_t)qv[e + 3] << 24);
+    r.s = s;
+  }
+  return r;
+}
+
+// Element e (0 <= e < D/32) of lane `lane`'s part of a quantised row, as stored.
+template <int KIND, int D>
+__device__ __forceinline__ uint32_t row_elem(const RowQ<KIND, D>& r, int e) {
+  if constexpr (KIND == kRowsF16) {
+    return (r.w[e / 2] >> (16 * (e & 1))) & 0xffffu;
+  } else {
+    return (r.w[e / 4] >> (8 * (e & 3))) & 0xffu;
+  }
+}
+
+// Store lane `lane`'s part of a quantised row into the paged cache: page row `page`
+// (= block * kv_heads + kv_head), token offset `off` inside the block. Lane 0 writes the
+// scale slot (one-byte caches).
+//   K page [D/8][bs][8]: a lane's values lie inside one 8-wide chunk (one store);
+//   V page [D][bs]:      one element per head_dim row.
+template <int KIND, int D>
+__device__ __forceinline__ void store_row(const RowQ<KIND, D>& r, int lane, bool is_v,
+                                          void* cache, float* scales, size_t page, int off,
+                                          int bs) {
+  constexpr int DPL = D / 32;
+  const int d0 = lane * DPL;
+  constexpr int ES = KIND == kRowsF16 ? 2 : 1;
+  uint8_t* c = reinterpret_cast<uint8_t*>(cache);
+  if (!is_v) {
+    uint8_t* dst = c + ((page * (D / 8) + d0 / 8) * bs * 8 + (size_t)off * 8 + (d0 & 7)) * ES;
+    if constexpr (KIND == kRowsF16 && DPL == 4) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(r.w[0], r.w[1]);
+    } else if constexpr (KIND != kRowsF16 && DPL == 4) {
+      *reinterpret_cast<uint32_t*>(dst) = r.w[0];
     } else {
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) c[(page * D + d0 + e) * bs + off] = qv[e];
+      for (int e = 0; e < DPL; ++e) {
+        if constexpr (ES == 2) {
+          reinterpret_cast<uint16_t*>(dst)[e] = (uint16_t)row_elem<KIND, D>(r, e);
+        } else {
+          dst[e] = (uint8_t)row_elem<KIND, D>(r, e);
+        }
+      }
     }
-    if (lane == 0) scales[page * bs + off] = s;
+  } else {
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      const size_t i = (page * D + d0 + e) * bs + off;
+      if constexpr (ES == 2) {
+        reinterpret_cast<uint16_t*>(c)[i] = (uint16_t)row_elem<KIND, D>(r, e);
+      } else {
+        c[i] = (uint8_t)row_elem<KIND, D>(r, e);
+      }
+    }
   }
+  if (KIND != kRowsF16 && lane == 0) scales[page * bs + off] = r.s;
+}
+
+// One warp writes one row (K or V) of one (token, kv head) into the paged cache.
+template <typename T, int KIND, int D>
+__device__ __forceinline__ void warp_write_row(const T* src, int lane, bool is_v, void* cache,
+                                               float* scales, size_t page, int off, int bs,
+                                               const float* fix) {
+  const RowQ<KIND, D> r = warp_quantize_row<T, KIND, D>(src, lane, fix);
+  store_row<KIND, D>(r, lane, is_v, cache, scales, page, off, bs);
 }
 
 }  // namespace pa

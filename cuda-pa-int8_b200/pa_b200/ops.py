@@ -117,10 +117,18 @@ def _kv_kind(k_cache, k_scales):
 _KV_CODE = {"f16": _lib.PA_DTYPE_F16, "i8": _lib.PA_DTYPE_I8, "f8": _lib.PA_DTYPE_FP8E4M3}
 
 
-def _check_lengths(context_lens, capacity):
-    """The reference's context_lens >= 1 check (and this library's upper bound), from one
-    device-to-host copy of the lengths; synchronises the current stream."""
-    cl = context_lens.cpu()
+def _check_lengths(context_lens, capacity, host_context_lens=None):
+    """The reference's context_lens >= 1 check (and this library's upper bound). It reads
+    host_context_lens, a CPU copy of the lengths, when the caller has one (no
+    synchronisation); otherwise one device-to-host copy of context_lens, which synchronises
+    the current stream."""
+    if host_context_lens is not None:
+        _require(host_context_lens.device.type == "cpu" and
+                 host_context_lens.numel() == context_lens.numel(),
+                 "host_context_lens must be a CPU tensor with one length per sequence")
+        cl = host_context_lens
+    else:
+        cl = context_lens.cpu()
     if cl.numel() == 0:
         return
     _require(int(cl.min()) >= 1, "context_lens must be >= 1 (empty sequences unsupported)")
@@ -189,7 +197,8 @@ def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, bloc
 
 
 def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16, *,
-           k_scales=None, v_scales=None, splitk=False, validate=True, kv_kind=None):
+           k_scales=None, v_scales=None, splitk=False, validate=True, kv_kind=None,
+           host_context_lens=None):
     """Paged decode attention into `out` (fp16 [num_seqs, num_heads, head_dim]).
 
     The cache type follows the tensors: fp16; int8 or float8_e4m3fn, each with per-token fp32
@@ -199,6 +208,9 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
     that checks context_lens (the kernels still flag bad lengths in the status word).
     kv_kind ('f16', 'i8' or 'f8') pins the cache type instead of inferring it from the
     tensors, so a cache of another type is rejected (the reference-named ops use this).
+    host_context_lens, a CPU tensor holding the same lengths (for instance the pinned copy the
+    lengths were uploaded from), moves that check to the host: the call then does not
+    synchronise.
     """
     kind = kv_kind or _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
@@ -228,16 +240,17 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
             args = (out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                     block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D, NB,
                     block_size, max_blocks, float(scale), ws.data_ptr(), ws.numel(), stream)
-        # The one host sync comes last, so the launch follows it with no Python work between.
+        # The one host sync (if any) comes last, so the launch follows it with no Python work
+        # between.
         if validate:
-            _check_lengths(context_lens, max_blocks * block_size)
+            _check_lengths(context_lens, max_blocks * block_size, host_context_lens)
         _lib.check(fn(*args), "paged decode")
     return out
 
 
 def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_lens, scale,
                 block_size=16, *, k_scales=None, v_scales=None, k_scale=None, v_scale=None,
-                splitk=False, fused=True, validate=True):
+                splitk=False, fused=True, validate=True, host_context_lens=None):
     """One decode step: append every sequence's new token to the cache, then decode.
 
     context_lens already counts the new token: new_k / new_v [num_seqs, kv_heads, head_dim]
@@ -253,7 +266,8 @@ def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_len
 
     With validate=False the call does no host synchronisation and allocates nothing once the
     stream's workspace exists, so after one call on a stream it can be captured in a CUDA
-    graph (the kernels still flag bad lengths in the status word).
+    graph (the kernels still flag bad lengths in the status word). host_context_lens (a CPU
+    copy of the lengths) checks them on the host without synchronising, as in decode().
     """
     kind = _kv_kind(k_cache, k_scales)
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
@@ -285,7 +299,7 @@ def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_len
                 block_size, max_blocks, float(scale), 1 if splitk else 0, 1 if fused else 0,
                 ws.data_ptr(), ws.numel(), _stream(q.device))
         if validate:
-            _check_lengths(context_lens, max_blocks * block_size)
+            _check_lengths(context_lens, max_blocks * block_size, host_context_lens)
         _lib.check(L.pa_decode_step(*args), "paged decode step")
     return out
 
