@@ -18,10 +18,12 @@
 //    (the split-K pair); partial mode writes one merged partial per segment (cross-GPU).
 //  * All q heads of a GQA group share one pass over the K/V page: QK^T and PV run on the
 //    tensor cores (mma.sync m16n8k16, f16 in / f32 accumulate) with heads on the MMA rows
-//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8 and FP8 K/V
-//    bytes convert to fp16 exactly in registers (int8: magic-exponent unpack; e4m3: hardware
-//    e4m3x2 -> f16x2), so every QK product is exact. The per-token K scale multiplies the
-//    dot product and the per-token V scale is folded into the softmax weight (the dequant
+//    (QK) or columns (PV), so K and V are read from HBM once per kv-head. INT8: QK runs on
+//    the integer tensor cores (m16n8k32) on the raw K bytes against q written exactly enough
+//    as three int8 parts over a power-of-two scale; V bytes unpack to exact fp16 integers in
+//    registers. FP8: K and V bytes convert to fp16 exactly (hardware e4m3x2 -> f16x2). The
+//    per-token K scale multiplies the dot product and the per-token V scale is folded into
+//    the softmax weight (the dequant
 //    fusion of kernels/paged_attention_v5_warp_int8.cu:82-85,101-108); the weights enter the
 //    PV MMA as two fp16 parts (hi + lo), so the output tracks the reference's fp32 arithmetic
 //    to about 1e-5 even where attention concentrates on a few large V entries.
@@ -584,6 +586,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ int s_ctx[kBMax];
   __shared__ int s_tmp[32];
   __shared__ int s_empty;
+  __shared__ unsigned s_over[kBMax / 32];  // sequences whose context exceeds the table
   __shared__ int s_pend[WARPS][2][6];
   __shared__ int s_npend[WARPS];
   __shared__ int s_wrow[WARPS][DEPTH];  // decode step: page row whose new token a stage holds
@@ -635,6 +638,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int SEGS = a.KVH * a.HT;
   const int cap = a.max_blocks * a.bs;
   int carry = 0;
+  for (int i = threadIdx.x; i < kBMax / 32; i += NTHR) s_over[i] = 0u;
   __syncthreads();
   for (int base = 0; base < a.B; base += NTHR) {
     const int b = base + threadIdx.x;
@@ -649,6 +653,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
       if (c > cap) {
         if (blockIdx.x == 0) flag_error(a.status, PA_ERR_CONTEXT_RANGE);
+        atomicOr(&s_over[b >> 5], 1u << (b & 31));
         c = cap;
       }
       s_ctx[b] = c;
@@ -751,12 +756,21 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   int cctx = s_ctx[cb];
   const float qs = a.qk_scale_log2;
 
-  // Q fragments: fp16 A fragments of the m16n8k16 MMA (qa rows g, qb rows g+8), loaded in
-  // the chunk order of the cache's K tile layout. K is fp16 in every QK product (int8 and e4m3
-  // bytes convert to fp16 exactly), so the products are exact and sum in fp32, as in the
-  // reference's fp32 dequantised attention.
+  // Q fragments, loaded in the chunk order of the cache's K tile layout (qa rows g, qb rows
+  // g+8 of the MMA).
+  // FP16 and FP8 caches: fp16 A fragments of the m16n8k16 MMA; e4m3 K bytes convert to fp16
+  // exactly, so every QK product is exact and sums in fp32.
+  // INT8 cache: the integer tensor cores (m16n8k32) take the raw K bytes, against q written as
+  // three int8 parts over a power-of-two scale s_q = 2^(e-6), 2^e > max|q|:
+  //   t = q / s_q (exact, |t| < 64), q1 = rint(t), q2 = rint(128 (t - q1)),
+  //   q3 = rint(128 (128 (t - q1) - q2))          (every product and difference exact),
+  // q = s_q (q1 + q2/128 + q3/16384) to within 2^-15 s_q, which is exact for every entry within
+  // a factor 2^10 of max|q| and below 1e-6 max|q| for the rest; the three integer dot
+  // products are exact. qa = {q1 lo, q1 hi, q2 lo, q2 hi}, qc / qd = {q3 lo, q3 hi}.
   uint4 qa[NS], qb[NS];
+  uint2 qc[NS], qd[NS];
   uint4 ra[NS], rb[NS];  // q rows fetched ahead of the piece that uses them
+  float qsc0 = 0.f, qsc1 = 0.f;
   int q_b = -1, q_seg = -1;
 
   auto fetch_q = [&](int b, int seg) {
@@ -777,11 +791,72 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   };
-  auto convert_q = [&]() {
+  auto split_row = [&](const uint4 (&src)[NS], uint4 (&dst)[NS], uint2 (&dst3)[NS],
+                       float& qsc) {
+    float amax = 0.f;
 #pragma unroll
     for (int si = 0; si < NS; ++si) {
-      qa[si] = ra[si];
-      qb[si] = rb[si];
+      const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    // 2^e > amax (e from amax's exponent field); s_q = 2^(e-6), inv = 2^(6-e). A zero row
+    // keeps s_q = 1 and all-zero parts.
+    const int e2 = amax > 0.f ? ((__float_as_int(amax) >> 23) & 0xff) - 126 : 6;
+    qsc = __int_as_float((127 + e2 - 6) << 23);
+    const float inv = __int_as_float((127 + 6 - e2) << 23);
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
+      int q1[8], q2[8], q3[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+        const float tt[2] = {f.x * inv, f.y * inv};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float t = tt[h];
+          const float p1 = rintf(t);
+          const float r1 = (t - p1) * 128.f;
+          const float p2 = rintf(r1);
+          const float p3 = rintf((r1 - p2) * 128.f);
+          q1[2 * e + h] = (int)p1;
+          q2[2 * e + h] = (int)p2;
+          q3[2 * e + h] = (int)p3;
+        }
+      }
+      dst[si] = make_uint4(pack_s8x4(q1[0], q1[1], q1[2], q1[3]),
+                           pack_s8x4(q1[4], q1[5], q1[6], q1[7]),
+                           pack_s8x4(q2[0], q2[1], q2[2], q2[3]),
+                           pack_s8x4(q2[4], q2[5], q2[6], q2[7]));
+      dst3[si] = make_uint2(pack_s8x4(q3[0], q3[1], q3[2], q3[3]),
+                            pack_s8x4(q3[4], q3[5], q3[6], q3[7]));
+    }
+  };
+
+  auto convert_q = [&]() {
+    if constexpr (I8) {
+      split_row(ra, qa, qc, qsc0);
+      if constexpr (GT == 16) {
+        split_row(rb, qb, qd, qsc1);
+      } else {
+#pragma unroll
+        for (int si = 0; si < NS; ++si) {
+          qb[si] = make_uint4(0u, 0u, 0u, 0u);
+          qd[si] = make_uint2(0u, 0u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int si = 0; si < NS; ++si) {
+        qa[si] = ra[si];
+        qb[si] = rb[si];
+      }
     }
   };
   // The first piece's q rows are requested before the page copies, so their latency overlaps
@@ -813,7 +888,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         ok = false;
       }
       pk = ((blk * a.KVH + kvh) << 3) | sub;
-      if (step_write && ok && sp == pages_of(b) - 1 && __ldg(a.context_lens + b) <= cap) wr = b;
+      if (step_write && ok && sp == pages_of(b) - 1 && !((s_over[b >> 5] >> (b & 31)) & 1u))
+        wr = b;
     }
     return pk;
   };
@@ -1036,20 +1112,82 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       // S = Q K^T : rows = heads (g, g+8), columns = tokens tok(jt, n); tokens 4r..4r+3 of
       // head g end up in x[0..3] (and of head g+8 in y[0..3]).
       float x[4], y[4];
-      {
-        if constexpr (BYTE) {
-          // int8 (magic-exponent unpack) or e4m3 K bytes -> exact fp16.
+      if constexpr (I8) {
+        // Three exact integer dot products per (head, token) on the raw K bytes, combined as
+        // s_q (p1 + p2/128 + p3/16384).
+        constexpr float k2 = 1.f / 128.f, k3 = 1.f / 16384.f;
+        if constexpr (NT == 1) {
+          // Eight heads leave the MMA's rows 8-15 free: they take q's second part, so one MMA
+          // gives p1 (rows g) and p2 (rows g+8) and a second one p3.
+          int s12[2][4], s3[2][4];
+#pragma unroll
+          for (int jt = 0; jt < 2; ++jt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              s12[jt][e] = 0;
+              s3[jt][e] = 0;
+            }
+#pragma unroll
+          for (int si = 0; si < NS; ++si) {
+#pragma unroll
+            for (int jt = 0; jt < 2; ++jt) {
+              imma_16832(s12[jt], qa[si].x, qa[si].z, qa[si].y, qa[si].w, k8[si][jt].x,
+                         k8[si][jt].y);
+              imma_16832(s3[jt], qc[si].x, 0u, qc[si].y, 0u, k8[si][jt].x, k8[si][jt].y);
+            }
+          }
+#pragma unroll
+          for (int jt = 0; jt < 2; ++jt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+              x[2 * jt + e] = fmaf((float)s3[jt][e], k3,
+                                   fmaf((float)s12[jt][2 + e], k2, (float)s12[jt][e])) *
+                              qsc0;
+          y[0] = y[1] = y[2] = y[3] = 0.f;
+        } else {
+          int sa[2][4], sb2[2][4], sc3[2][4];
+#pragma unroll
+          for (int jt = 0; jt < 2; ++jt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              sa[jt][e] = 0;
+              sb2[jt][e] = 0;
+              sc3[jt][e] = 0;
+            }
+#pragma unroll
+          for (int si = 0; si < NS; ++si) {
+#pragma unroll
+            for (int jt = 0; jt < 2; ++jt) {
+              imma_16832(sa[jt], qa[si].x, qb[si].x, qa[si].y, qb[si].y, k8[si][jt].x,
+                         k8[si][jt].y);
+              imma_16832(sb2[jt], qa[si].z, qb[si].z, qa[si].w, qb[si].w, k8[si][jt].x,
+                         k8[si][jt].y);
+              imma_16832(sc3[jt], qc[si].x, qd[si].x, qc[si].y, qd[si].y, k8[si][jt].x,
+                         k8[si][jt].y);
+            }
+          }
+          auto comb = [&](int jt, int e, float qsc) {
+            return fmaf((float)sc3[jt][e], k3,
+                        fmaf((float)sb2[jt][e], k2, (float)sa[jt][e])) * qsc;
+          };
+          x[0] = comb(0, 0, qsc0);
+          x[1] = comb(0, 1, qsc0);
+          x[2] = comb(1, 0, qsc0);
+          x[3] = comb(1, 1, qsc0);
+          y[0] = comb(0, 2, qsc1);
+          y[1] = comb(0, 3, qsc1);
+          y[2] = comb(1, 2, qsc1);
+          y[3] = comb(1, 3, qsc1);
+        }
+      } else {
+        if constexpr (F8) {
+          // e4m3 K bytes -> exact fp16.
 #pragma unroll
           for (int si = 0; si < NS; ++si)
 #pragma unroll
             for (int jt = 0; jt < 2; ++jt) {
-              if constexpr (I8) {
-                i8x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
-                i8x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
-              } else {
-                e4m3x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
-                e4m3x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
-              }
+              e4m3x4_to_f16x2x2(k8[si][jt].x, k16[si][jt].x, k16[si][jt].y);
+              e4m3x4_to_f16x2x2(k8[si][jt].y, k16[si][jt].z, k16[si][jt].w);
             }
         }
         // Two accumulation chains per n-tile (even / odd si) shorten the MMA dependency.
