@@ -564,6 +564,58 @@ __device__ __forceinline__ void group_combine(PieceFn piece, int np, int hcnt, _
 }
 
 // ---------------------------------------------------------------------------------------
+// Decode step: the new token's rows in a stage (bulk-copied with the page, rk = K row then V
+// row, 16-bit) are quantised like the cache writes, placed into the staged page at token t of
+// the subpage (the copy brought the slot's previous contents), and stored into the cache at
+// page row `row`, offset `off` for later steps. Only the calling warp reads the page, so
+// nothing orders the global stores against the copies. Kept out of line: it runs once per
+// segment, and inlined into the page loop it made every page slower.
+// ---------------------------------------------------------------------------------------
+template <int KVK, int D>
+__device__ __noinline__ void stage_new_token(const uint8_t* rk, uint8_t* kt, uint8_t* vt,
+                                             uint8_t* sd, int lane, int row, int t, int off,
+                                             int new_dtype, const float* kfix,
+                                             const float* vfix, void* kc, void* vc, float* ks,
+                                             float* vs, int bs) {
+  static_assert(D == 128, "one lane per four head_dim values");
+  constexpr bool BYTE = KVK != 0;
+  constexpr int KIND = KVK == 1 ? kRowsI8 : (KVK == 2 ? kRowsFP8 : kRowsF16);
+  RowQ<KIND, D> qk, qv;
+  if (new_dtype == PA_DTYPE_BF16) {
+    qk = warp_quantize_row<__nv_bfloat16, KIND, D>(reinterpret_cast<const __nv_bfloat16*>(rk),
+                                                   lane, kfix);
+    qv = warp_quantize_row<__nv_bfloat16, KIND, D>(
+        reinterpret_cast<const __nv_bfloat16*>(rk + D * 2), lane, vfix);
+  } else {
+    qk = warp_quantize_row<__half, KIND, D>(reinterpret_cast<const __half*>(rk), lane, kfix);
+    qv = warp_quantize_row<__half, KIND, D>(reinterpret_cast<const __half*>(rk + D * 2), lane,
+                                            vfix);
+  }
+  const int c = lane >> 1;  // the 8-wide head_dim chunk of this lane's four values
+  if constexpr (BYTE) {
+    const int o = c * 128 + ((((t >> 1) ^ (c & 7)) << 4) | ((t & 1) << 3)) + 4 * (lane & 1);
+    *reinterpret_cast<uint32_t*>(kt + o) = qk.w[0];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) vt[(4 * lane + e) * kSubTokens + t] = (uint8_t)row_elem(qv, e);
+    if (lane == 0) {
+      reinterpret_cast<float*>(sd)[t] = qk.s;
+      reinterpret_cast<float*>(sd + kVsOff)[t] = qv.s;
+    }
+  } else {
+    const int rr = 2 * c + (t >> 3);
+    const int o = rr * 128 + (((t & 7) ^ (rr & 7)) << 4) + 8 * (lane & 1);
+    *reinterpret_cast<uint2*>(kt + o) = make_uint2(qk.w[0], qk.w[1]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      reinterpret_cast<uint16_t*>(vt)[(4 * lane + e) * kSubTokens + t] =
+          (uint16_t)row_elem(qv, e);
+  }
+  store_row(qk, lane, false, kc, ks, (size_t)row, off, bs);
+  store_row(qv, lane, true, vc, vs, (size_t)row, off, bs);
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------------------
 // The decode kernel.
 // ---------------------------------------------------------------------------------------
 template <int KVK, int D, int GT, int DEPTH, int WARPS>
@@ -978,52 +1030,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const uint32_t vbase = smem_u32(v_tiles) + warp * DEPTH * C::VT;
   const uint32_t sbase = BYTE ? smem_u32(s_tiles) + warp * DEPTH * C::ST : 0u;
 
-  // Decode step: the new token's rows in stage s (bulk-copied with the page) are quantised
-  // like the cache writes, placed into the staged page at token t of the subpage (the TMA
-  // brought the slot's previous contents), and stored into the cache at page row `row`,
-  // offset `off` for later steps. Only this warp reads the page, so nothing orders the
-  // global stores against the copies.
+  // Decode step: the new token held in stage st goes into the staged page and the cache.
   auto merge_new_token = [&](int st, int row, int t, int off) {
-    static_assert(D == 128, "one lane per four head_dim values");
-    constexpr int KIND = I8 ? kRowsI8 : (F8 ? kRowsFP8 : kRowsF16);
-    const uint8_t* rk = r_tiles + (warp * DEPTH + st) * C::NR;
-    RowQ<KIND, D> qk, qv;
-    if (a.new_dtype == PA_DTYPE_BF16) {
-      qk = warp_quantize_row<__nv_bfloat16, KIND, D>(
-          reinterpret_cast<const __nv_bfloat16*>(rk), lane, a.new_kfix);
-      qv = warp_quantize_row<__nv_bfloat16, KIND, D>(
-          reinterpret_cast<const __nv_bfloat16*>(rk + D * 2), lane, a.new_vfix);
-    } else {
-      qk = warp_quantize_row<__half, KIND, D>(reinterpret_cast<const __half*>(rk), lane,
-                                              a.new_kfix);
-      qv = warp_quantize_row<__half, KIND, D>(reinterpret_cast<const __half*>(rk + D * 2),
-                                              lane, a.new_vfix);
-    }
-    uint8_t* kt = k_tiles + (warp * DEPTH + st) * C::KT;
-    uint8_t* vt = v_tiles + (warp * DEPTH + st) * C::VT;
-    const int c = lane >> 1;  // the 8-wide head_dim chunk of this lane's four values
-    if constexpr (BYTE) {
-      const int o = c * 128 + ((((t >> 1) ^ (c & 7)) << 4) | ((t & 1) << 3)) + 4 * (lane & 1);
-      *reinterpret_cast<uint32_t*>(kt + o) = qk.w[0];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vt[(4 * lane + e) * kSubTokens + t] = (uint8_t)row_elem(qv, e);
-      if (lane == 0) {
-        uint8_t* sd = s_tiles + (warp * DEPTH + st) * C::ST;
-        reinterpret_cast<float*>(sd)[t] = qk.s;
-        reinterpret_cast<float*>(sd + kVsOff)[t] = qv.s;
-      }
-    } else {
-      const int rr = 2 * c + (t >> 3);
-      const int o = rr * 128 + (((t & 7) ^ (rr & 7)) << 4) + 8 * (lane & 1);
-      *reinterpret_cast<uint2*>(kt + o) = make_uint2(qk.w[0], qk.w[1]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        reinterpret_cast<uint16_t*>(vt)[(4 * lane + e) * kSubTokens + t] =
-            (uint16_t)row_elem(qv, e);
-    }
-    store_row(qk, lane, false, a.kc_w, a.ks_w, (size_t)row, off, a.bs);
-    store_row(qv, lane, true, a.vc_w, a.vs_w, (size_t)row, off, a.bs);
-    __syncwarp();
+    stage_new_token<KVK, D>(r_tiles + (warp * DEPTH + st) * C::NR,
+                            k_tiles + (warp * DEPTH + st) * C::KT,
+                            v_tiles + (warp * DEPTH + st) * C::VT,
+                            BYTE ? s_tiles + (warp * DEPTH + st) * C::ST : nullptr, lane, row, t,
+                            off, a.new_dtype, a.new_kfix, a.new_vfix, a.kc_w, a.vc_w, a.ks_w,
+                            a.vs_w, a.bs);
   };
 
   float m0 = neg_inf(), l0 = 0.f, m1 = neg_inf(), l1 = 0.f;
