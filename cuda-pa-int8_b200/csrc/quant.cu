@@ -76,23 +76,48 @@ __global__ void __launch_bounds__(256) step_rows_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
-// Block-granular prefill: one CTA per (block j, kv-head, sequence). Quantises (or rounds)
-// the block's tokens into shared memory, then writes the K page, the V page and the scales
-// with 16-byte stores. Tokens past the context are written as zeros with scale 0.
+// Block-granular prefill: one CTA per (block j, kv-head, sequence). The block's K and V rows
+// are loaded with one vector load per lane and row, several rows in flight per warp, quantised
+// (or rounded) into shared memory, and written as whole K and V pages with 16-byte stores,
+// then the scales. Tokens past the context are written as zeros with scale 0.
 // ---------------------------------------------------------------------------------------
+constexpr int kPrefillThreads = 256;
+
+// The four consecutive input values of one lane (8 bytes for 16-bit inputs, 16 for fp32).
+__device__ __forceinline__ void load4(const __half* p, float (&x)[4]) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&x)[4]) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+}
+__device__ __forceinline__ void load4(const float* p, float (&x)[4]) {
+  const float4 u = __ldg(reinterpret_cast<const float4*>(p));
+  x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+}
+
 template <typename T, bool I8, int D>
-__global__ void __launch_bounds__(128) prefill_kernel(
+__global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int L, int KVH,
     const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
     void* __restrict__ k_cache, void* __restrict__ v_cache, float* __restrict__ k_scales,
     float* __restrict__ v_scales, int NB, int bs, const float* __restrict__ kfix,
     const float* __restrict__ vfix, int* status) {
+  static_assert(D == 128, "a lane loads four consecutive head_dim values");
   using OutT = typename std::conditional<I8, int8_t, __half>::type;
-  constexpr int DPL = D / 32;
   constexpr int ELEM = sizeof(OutT);
+  constexpr int NW = kPrefillThreads / 32;
+  constexpr int RB = 4;  // rows per warp whose loads are in flight together
   extern __shared__ __align__(16) uint8_t sm[];
-  OutT* q_sm = reinterpret_cast<OutT*>(sm);                     // [bs][D]
-  float* s_sm = reinterpret_cast<float*>(sm + (size_t)bs * D * ELEM);  // [bs]
+  OutT* kq = reinterpret_cast<OutT*>(sm);                              // [bs][D]
+  OutT* vq = kq + (size_t)bs * D;                                      // [bs][D]
+  float* ksm = reinterpret_cast<float*>(sm + 2 * (size_t)bs * D * ELEM);  // [bs]
+  float* vsm = ksm + bs;                                               // [bs]
 
   const int j = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -116,18 +141,29 @@ __global__ void __launch_bounds__(128) prefill_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t page = (size_t)blk * KVH + kvh;
 
-  for (int which = 0; which < 2; ++which) {
-    const T* src = which ? v : k;
-    const float* fix = which ? vfix : kfix;
-    for (int i = warp; i < bs; i += 4) {
-      float x[DPL];
-      if (i < valid) {
-        load_vals<T, DPL>(src + (((size_t)b * L + t0 + i) * KVH + kvh) * D + lane * DPL, x);
+  // Rows 0 .. bs-1 are K rows, bs .. 2bs-1 V rows; warp w takes rows w, w + NW, ...
+  for (int r0 = warp; r0 < 2 * bs; r0 += NW * RB) {
+    float x[RB][4];
+#pragma unroll
+    for (int rb = 0; rb < RB; ++rb) {
+      const int r = r0 + rb * NW;
+      const int i = r < bs ? r : r - bs;
+      if (r < 2 * bs && i < valid) {
+        load4((r < bs ? k : v) + (((size_t)b * L + t0 + i) * KVH + kvh) * D + lane * 4, x[rb]);
       } else {
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) x[e] = 0.f;
+        for (int e = 0; e < 4; ++e) x[rb][e] = 0.f;
       }
+    }
+#pragma unroll
+    for (int rb = 0; rb < RB; ++rb) {
+      const int r = r0 + rb * NW;
+      if (r >= 2 * bs) break;  // uniform across the warp
+      const bool is_v = r >= bs;
+      const int i = is_v ? r - bs : r;
+      OutT* q = (is_v ? vq : kq) + (size_t)i * D + lane * 4;
       if constexpr (I8) {
+        const float* fix = is_v ? vfix : kfix;
         float s;
         if (i >= valid) {
           s = 0.f;
@@ -136,24 +172,30 @@ __global__ void __launch_bounds__(128) prefill_kernel(
         } else {
           float am = 0.f;
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) am = fmaxf(am, fabsf(x[e]));
+          for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(x[rb][e]));
           am = warp_max(am);
           s = token_scale<T>(am);
         }
+        int8_t qv[4];
 #pragma unroll
-        for (int e = 0; e < DPL; ++e)
-          q_sm[i * D + lane * DPL + e] = (i < valid) ? quant1(x[e], s) : (int8_t)0;
-        if (lane == 0) s_sm[i] = s;
+        for (int e = 0; e < 4; ++e) qv[e] = (i < valid) ? quant1(x[rb][e], s) : (int8_t)0;
+        *reinterpret_cast<uint32_t*>(q) = *reinterpret_cast<const uint32_t*>(qv);
+        if (lane == 0) (is_v ? vsm : ksm)[i] = s;
       } else {
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) q_sm[i * D + lane * DPL + e] = __float2half_rn(x[e]);
+        const __half2 h0 = __floats2half2_rn(x[rb][0], x[rb][1]);
+        const __half2 h1 = __floats2half2_rn(x[rb][2], x[rb][3]);
+        *reinterpret_cast<uint2*>(q) = make_uint2(*reinterpret_cast<const uint32_t*>(&h0),
+                                                  *reinterpret_cast<const uint32_t*>(&h1));
       }
     }
-    __syncthreads();
-    OutT* cache = reinterpret_cast<OutT*>(which ? v_cache : k_cache);
-    OutT* pg = cache + page * (size_t)D * bs;
-    constexpr int PER16 = 16 / ELEM;  // elements per 16-byte store
-    const int units = D * bs / PER16;
+  }
+  __syncthreads();
+
+  constexpr int PER16 = 16 / ELEM;  // elements per 16-byte store
+  const int units = D * bs / PER16;
+  for (int which = 0; which < 2; ++which) {
+    const OutT* q_sm = which ? vq : kq;
+    OutT* pg = reinterpret_cast<OutT*>(which ? v_cache : k_cache) + page * (size_t)D * bs;
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
       alignas(16) OutT tmp[PER16];
       const int e0 = u * PER16;  // element offset inside the page
@@ -180,11 +222,12 @@ __global__ void __launch_bounds__(128) prefill_kernel(
       }
       *reinterpret_cast<uint4*>(pg + e0) = *reinterpret_cast<const uint4*>(tmp);
     }
-    if constexpr (I8) {
-      float* sc = (which ? v_scales : k_scales) + page * bs;
-      for (int t = threadIdx.x; t < bs; t += blockDim.x) sc[t] = s_sm[t];
+  }
+  if constexpr (I8) {
+    for (int t = threadIdx.x; t < 2 * bs; t += blockDim.x) {
+      if (t < bs) k_scales[page * bs + t] = ksm[t];
+      else v_scales[page * bs + t - bs] = vsm[t - bs];
     }
-    __syncthreads();
   }
 }
 
@@ -273,16 +316,16 @@ cudaError_t launch_prefill_t(bool i8, const void* k, const void* v, int S, int L
   const dim3 grid(max_blocks, KVH, S);
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
-  if (i8) {
-    const size_t smem = (size_t)bs * 128 + bs * 4;
-    prefill_kernel<T, true, 128><<<grid, 128, smem, st>>>(kk, vv, L, KVH, bt, cl, max_blocks, kc,
-                                                          vc, ks, vs, NB, bs, kf, vf, status);
-  } else {
-    const size_t smem = (size_t)bs * 128 * 2 + bs * 4;
-    prefill_kernel<T, false, 128><<<grid, 128, smem, st>>>(kk, vv, L, KVH, bt, cl, max_blocks,
-                                                           kc, vc, ks, vs, NB, bs, kf, vf,
-                                                           status);
+  // Shared memory: the quantised K and V rows of one block plus their scales.
+  const size_t smem = 2 * (size_t)bs * 128 * (i8 ? 1 : 2) + 2 * (size_t)bs * 4;
+  auto kern = i8 ? prefill_kernel<T, true, 128> : prefill_kernel<T, false, 128>;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
   }
+  kern<<<grid, kPrefillThreads, smem, st>>>(kk, vv, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs,
+                                            NB, bs, kf, vf, status);
   return cudaGetLastError();
 }
 
