@@ -131,8 +131,9 @@ def _check_lengths(context_lens, capacity, host_context_lens=None):
         cl = context_lens.cpu()
     if cl.numel() == 0:
         return
-    _require(int(cl.min()) >= 1, "context_lens must be >= 1 (empty sequences unsupported)")
-    _require(int(cl.max()) <= capacity, "context_lens exceeds max_blocks_per_seq * block_size")
+    a = cl.numpy()  # a view: numpy's reductions cost less per call than torch's on the CPU
+    _require(int(a.min()) >= 1, "context_lens must be >= 1 (empty sequences unsupported)")
+    _require(int(a.max()) <= capacity, "context_lens exceeds max_blocks_per_seq * block_size")
 
 
 def _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens, block_size,
@@ -246,6 +247,74 @@ def decode(out, q, k_cache, v_cache, block_table, context_lens, scale, block_siz
             _check_lengths(context_lens, max_blocks * block_size, host_context_lens)
         _lib.check(fn(*args), "paged decode")
     return out
+
+
+class DecodePlan:
+    """decode() for a serving loop: the argument checks run once, at construction.
+
+    Construction takes the same arguments as decode() and validates them the same way; it
+    resolves the entry point, the launch sizes and the cache pointers. run() launches the
+    decode on the current stream, with the tensors given at construction or, per call, other
+    out / q / block_table / context_lens tensors of the same shape, dtype and device (checked
+    cheaply; anything else raises RuntimeError). The cache tensors stay those of construction.
+    Results are identical to decode()'s. host_context_lens / validate behave as in decode().
+    """
+
+    def __init__(self, out, q, k_cache, v_cache, block_table, context_lens, scale, block_size=16,
+                 *, k_scales=None, v_scales=None, splitk=False):
+        kind = _kv_kind(k_cache, k_scales)
+        B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table,
+                                              context_lens, block_size, kind, k_scales,
+                                              v_scales)
+        L = _lib.lib()
+        self.max_blocks = block_table.shape[1]
+        kv = _KV_CODE[kind]
+        self.need = L.pa_decode_workspace_bytes(B, H, KVH, D, self.max_blocks, block_size, kv,
+                                                1 if splitk else 0)
+        _require(B == 0 or self.need > 0, "unsupported decode shape: " + _lib.last_error())
+        if kind == "f8":
+            self.fn = L.pa_splitk_fp8 if splitk else L.pa_decode_fp8
+        elif kind == "i8":
+            self.fn = L.pa_splitk_i8 if splitk else L.pa_decode_i8
+        else:
+            self.fn = L.pa_splitk_f16 if splitk else L.pa_decode_f16
+        self.scaled = kind != "f16"
+        self.device = q.device
+        self.sizes = (B, H, KVH, D, NB, block_size, self.max_blocks, float(scale))
+        self.caches = ((k_cache.data_ptr(), v_cache.data_ptr()) +
+                       ((k_scales.data_ptr(), v_scales.data_ptr()) if self.scaled else ()))
+        self._keep = (k_cache, v_cache, k_scales, v_scales)  # the cache tensors stay alive
+        self.capacity = self.max_blocks * block_size
+        self.tensors = [out, q, block_table, context_lens]
+        self.specs = [(tuple(t.shape), t.dtype) for t in self.tensors]
+
+    def _match(self, i, t):
+        if t is None:
+            return self.tensors[i]
+        shape, dtype = self.specs[i]
+        _require(t.dtype == dtype and tuple(t.shape) == shape and t.device == self.device and
+                 t.is_contiguous(),
+                 "DecodePlan.run: tensors must match the plan's shapes, dtypes and device")
+        return t
+
+    def run(self, out=None, q=None, block_table=None, context_lens=None, *,
+            host_context_lens=None, validate=True):
+        out, q = self._match(0, out), self._match(1, q)
+        block_table, context_lens = self._match(2, block_table), self._match(3, context_lens)
+        B, H, KVH, D, NB, bs, mb, scale = self.sizes
+        if B == 0:
+            return out
+        with _Guard(self.device):
+            ws = workspace(self.device, self.need)
+            ptrs = (out.data_ptr(), q.data_ptr()) + self.caches[:2]
+            if self.scaled:
+                ptrs += self.caches[2:]
+            args = ptrs + (block_table.data_ptr(), context_lens.data_ptr(), B, H, KVH, D, NB,
+                           bs, mb, scale, ws.data_ptr(), ws.numel(), _stream(self.device))
+            if validate:
+                _check_lengths(context_lens, self.capacity, host_context_lens)
+            _lib.check(self.fn(*args), "paged decode")
+        return out
 
 
 def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_lens, scale,

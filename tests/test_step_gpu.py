@@ -282,3 +282,31 @@ def test_paged_cache_append_and_decode_matches_the_bridge_sequence():
             torch.cuda.synchronize()
             assert torch.equal(fused, ref), variant
         assert torch.equal(a.k_cache, b.k_cache) and torch.equal(a.v_cache, b.v_cache)
+
+
+def test_decode_plan_matches_decode_and_rejects_other_shapes():
+    """ops.DecodePlan: checks once, then run() equals decode() for the plan's tensors and for
+    other tensors of the same shapes; different shapes raise."""
+    from pa_b200 import ops
+    for kind in ("f16", "i8"):
+        c = _setup(kind, LENS, 12, 2, seed=21)
+        out = torch.empty_like(c["q"])
+        plan = ops.DecodePlan(out, c["q"], c["kc"], c["vc"], c["bt"], c["cl"], SCALE, 16,
+                              k_scales=c["ks"], v_scales=c["vs"])
+        plan.run(host_context_lens=c["cl"].cpu())
+        ref = torch.empty_like(out)
+        ops.decode(ref, c["q"], c["kc"], c["vc"], c["bt"], c["cl"], SCALE, 16,
+                   k_scales=c["ks"], v_scales=c["vs"])
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        q2 = torch.randn_like(c["q"])
+        out2 = torch.empty_like(out)
+        plan.run(out=out2, q=q2)
+        ops.decode(ref, q2, c["kc"], c["vc"], c["bt"], c["cl"], SCALE, 16, k_scales=c["ks"],
+                   v_scales=c["vs"])
+        torch.cuda.synchronize()
+        assert torch.equal(out2, ref)
+        with pytest.raises(RuntimeError, match="plan"):
+            plan.run(q=q2[:1].contiguous())
+        with pytest.raises(RuntimeError, match="context_lens must be >= 1"):
+            plan.run(host_context_lens=torch.zeros_like(c["cl"].cpu()))
