@@ -86,118 +86,92 @@ struct Tile {
 };
 
 // ---------------------------------------------------------------------------------------
-// Warp-level log-sum-exp merge for segments with few pieces (np <= 32): lane k reads piece
-// k's maxima and denominators; the O rows are then accumulated P pieces per step, each
-// lane owning head_dim rows [lane*D/32, (lane+1)*D/32). Several of these run in parallel,
-// one per warp.
+// Log-sum-exp merge of `np` partial slots by one warp, from copies of the slots in shared
+// memory: the lanes bulk-copy the slots into `stage` (np * SLOT floats) on the warp's
+// mbarrier `bar`, so a merge waits for one L2 round trip however many pieces it has. Sums
+// run in piece order (k = 0, 1, ...): the arithmetic, and the output's bits, are the same
+// whichever CTA performs the merge. Piece k of the segment is warp (wf + k)'s slot: slot
+// 2 (wf + k) + 1 for the first piece (it starts the segment), 2 (wf + k) for the others.
+// Returns false (status flagged) if the copies did not arrive within the wait limit; the
+// caller then stops using the staging memory. Out of line: it runs a few times per CTA at
+// the end of the launch and should not add to the page loop's registers.
 // ---------------------------------------------------------------------------------------
-// Largest merge a single warp takes; larger ones go to the four-warp groups, whose merges
-// need fewer dependent round trips. The routine is chosen from the piece count alone, so a
-// segment's summation order, and the output's bits, do not depend on which CTA happens to
-// finish the segment last.
-constexpr int kWarpMergeMax = 8;
+template <int D, int GT>
+__device__ __noinline__ bool staged_combine(const float* part, int wf, int np, int lane,
+                                            int hcnt, __half* out_rows, float* out_slot,
+                                            int* status, float* stage, uint64_t* bar,
+                                            uint32_t parity) {
+  constexpr int SLOT = (D + 2) * GT;
+  constexpr uint32_t SB = SLOT * sizeof(float);
+  constexpr int O4 = D * GT / 4 / 32;  // float4 outputs per lane
+  static_assert(D * GT / 4 % 32 == 0, "outputs must tile the warp");
+  // Earlier generic accesses (the ring's last reads, a previous merge's use of the staging
+  // memory, the acquire that made the slots visible) come before the copies.
+  fence_proxy_async_all();
+  if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)np * SB);
+  __syncwarp();
+  for (int k = lane; k < np; k += 32)
+    bulk_g2s(stage + (size_t)k * SLOT, part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT,
+             SB, bar);
+  if (!mbar_wait_bounded(bar, parity, status)) return false;
 
-template <int D, int GT, int P, typename PieceFn>
-__device__ __forceinline__ void warp_combine(PieceFn piece, int np, int lane, int hcnt,
-                                             __half* out_rows, float* out_slot, int* status) {
-  constexpr int DPL = D / 32;
-  constexpr int Q = DPL * GT / 4;
-  float mk[GT], lk[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    mk[h] = neg_inf();
-    lk[h] = 0.f;
-  }
-  if (lane < np) {
-    const float4* sl = reinterpret_cast<const float4*>(piece(lane) + D * GT);
-#pragma unroll
-    for (int h4 = 0; h4 < GT / 4; ++h4) {
-      const float4 m4 = __ldcg(sl + h4);
-      const float4 l4 = __ldcg(sl + GT / 4 + h4);
-      mk[4 * h4 + 0] = m4.x; mk[4 * h4 + 1] = m4.y; mk[4 * h4 + 2] = m4.z; mk[4 * h4 + 3] = m4.w;
-      lk[4 * h4 + 0] = l4.x; lk[4 * h4 + 1] = l4.y; lk[4 * h4 + 2] = l4.z; lk[4 * h4 + 3] = l4.w;
+  // Weights: lane h < GT takes head h, M = max_k m_k, w_k = 2^(m_k - M) (written over m_k in
+  // the staged slot), L = sum_k w_k l_k.
+  float Lh = 0.f, Mh = neg_inf();
+  if (lane < GT) {
+    for (int k = 0; k < np; ++k) Mh = fmaxf(Mh, stage[(size_t)k * SLOT + D * GT + lane]);
+    for (int k = 0; k < np; ++k) {
+      float* mk = stage + (size_t)k * SLOT + D * GT + lane;
+      const float w = (Mh == neg_inf()) ? 0.f : ex2(*mk - Mh);
+      *mk = w;
+      Lh = fmaf(w, mk[GT], Lh);
     }
   }
-  // O rows of P pieces per step (a piece past np reloads piece k and gets weight 0). The
-  // first step's loads do not depend on the weights, so they overlap the maxima's.
-  float4 v[P][Q];
-  auto load_step = [&](int k) {
+  __syncwarp();
+
+  // O = sum_k w_k O_k. Slots hold O as [D][GT]; float4 o covers row o / (GT/4), heads
+  // h0..h0+3 with h0 = 4 (o % (GT/4)), which is the same for all of a lane's outputs.
+  const int h0 = 4 * (lane % (GT / 4));
+  float4 acc[O4];
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const int kk = (k + p < np) ? k + p : k;
-      const float4* r = reinterpret_cast<const float4*>(piece(kk) + lane * DPL * GT);
+  for (int i = 0; i < O4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < np; ++k) {
+    const float* sk = stage + (size_t)k * SLOT;
+    const float4 w4 = *reinterpret_cast<const float4*>(sk + D * GT + h0);
 #pragma unroll
-      for (int q = 0; q < Q; ++q) v[p][q] = __ldcg(r + q);
-    }
-  };
-  load_step(0);
-  float wk[GT], L[GT], M[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    M[h] = warp_max(mk[h]);
-    wk[h] = (M[h] == neg_inf() || lane >= np) ? 0.f : ex2(mk[h] - M[h]);
-    float s = wk[h] * lk[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    L[h] = s;
-  }
-  float acc[DPL * GT];
-#pragma unroll
-  for (int i = 0; i < DPL * GT; ++i) acc[i] = 0.f;
-  for (int k = 0; k < np; k += P) {
-    if (k > 0) load_step(k);
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      const int h = (4 * q) % GT;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float s = 0.f;
-#pragma unroll
-        for (int p = 0; p < P; ++p) {
-          const float w = (k + p < np) ? __shfl_sync(0xffffffffu, wk[h + e], k + p) : 0.f;
-          const float x = e == 0 ? v[p][q].x : e == 1 ? v[p][q].y : e == 2 ? v[p][q].z
-                                                                         : v[p][q].w;
-          s += w * x;
-        }
-        acc[4 * q + e] += s;
-      }
+    for (int i = 0; i < O4; ++i) {
+      const float4 v = reinterpret_cast<const float4*>(sk)[lane + 32 * i];
+      acc[i].x = fmaf(w4.x, v.x, acc[i].x);
+      acc[i].y = fmaf(w4.y, v.y, acc[i].y);
+      acc[i].z = fmaf(w4.z, v.z, acc[i].z);
+      acc[i].w = fmaf(w4.w, v.w, acc[i].w);
     }
   }
   if (out_rows != nullptr) {
+    float inv[4];
 #pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      if (h < hcnt) {
-        float inv = 0.f;
-        if (L[h] > 0.f) {
-          inv = 1.f / L[h];
-        } else if (lane == 0) {
-          flag_error(status, PA_ERR_EMPTY_CONTEXT);
-        }
-        __half tmp[DPL];
+    for (int e = 0; e < 4; ++e) {
+      const float L = __shfl_sync(0xffffffffu, Lh, h0 + e);
+      inv[e] = L > 0.f ? 1.f / L : 0.f;
+    }
+    if (lane < hcnt && !(Lh > 0.f)) flag_error(status, PA_ERR_EMPTY_CONTEXT);
 #pragma unroll
-        for (int dd = 0; dd < DPL; ++dd) tmp[dd] = __float2half_rn(acc[dd * GT + h] * inv);
-        __half* dst = out_rows + (size_t)h * D + lane * DPL;
-        if constexpr (DPL == 4) {
-          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(tmp);
-        } else {
+    for (int i = 0; i < O4; ++i) {
+      const int d = (lane + 32 * i) / (GT / 4);
+      const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
 #pragma unroll
-          for (int dd = 0; dd < DPL; ++dd) dst[dd] = tmp[dd];
-        }
-      }
+      for (int e = 0; e < 4; ++e)
+        if (h0 + e < hcnt) out_rows[(size_t)(h0 + e) * D + d] = __float2half_rn(a4[e] * inv[e]);
     }
   } else {
-    float4* rows = reinterpret_cast<float4*>(out_slot + lane * DPL * GT);
 #pragma unroll
-    for (int q = 0; q < Q; ++q)
-      rows[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-    if (lane == 0) {
-#pragma unroll
-      for (int h = 0; h < GT; ++h) {
-        out_slot[D * GT + h] = M[h];
-        out_slot[D * GT + GT + h] = L[h];
-      }
+    for (int i = 0; i < O4; ++i) reinterpret_cast<float4*>(out_slot)[lane + 32 * i] = acc[i];
+    if (lane < GT) {
+      out_slot[D * GT + lane] = Mh;
+      out_slot[D * GT + GT + lane] = Lh;
     }
   }
+  return true;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -371,199 +345,6 @@ __device__ __forceinline__ void coop_combine(PieceFn piece, int np, int hcnt, __
 }
 
 // ---------------------------------------------------------------------------------------
-// Log-sum-exp merge of `np` partial slots by one group of GS threads (GS / 32 whole warps) of
-// the CTA, so that the few merges a CTA owes at the end of the launch run side by side
-// instead of one after another. The group synchronises on its own named barrier `bar_id`.
-// The maxima and denominators of all pieces and the O values of the first U pieces are
-// requested together, and the weights are formed from copies of the maxima in shared
-// memory, so a merge of up to U pieces costs one dependent L2 round trip before the output
-// is written (each further U pieces add one).
-// ---------------------------------------------------------------------------------------
-template <int D, int GT, int GS>
-struct Group {
-  static constexpr int OUT4 = D * GT / 4;  // float4 outputs of one merge
-  static_assert(OUT4 % GS == 0, "outputs must tile the group");
-  static constexpr int OPT = OUT4 / GS;    // outputs per thread
-  static constexpr int U = 16 / OPT;       // pieces per output in flight (16 float4 loads)
-  static constexpr int NWG = GS / 32;
-  // Scratch floats for np pieces: M, L, per-warp partials, then np x GT maxima (later the
-  // weights) and np x GT denominators.
-  __host__ __device__ static constexpr size_t floats(int np) {
-    return 2 * GT + NWG * GT + 2 * (((size_t)np * GT + 3) / 4 * 4);
-  }
-};
-
-// Named barriers 1..3 (barrier 0 is __syncthreads), with immediate ids so that the kernel
-// reserves only the barriers it uses.
-__device__ __forceinline__ void group_sync(int bar_id, int nthreads) {
-  if (bar_id == 1) {
-    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-  } else if (bar_id == 2) {
-    asm volatile("bar.sync 2, %0;" ::"r"(nthreads) : "memory");
-  } else {
-    asm volatile("bar.sync 3, %0;" ::"r"(nthreads) : "memory");
-  }
-}
-
-template <int D, int GT, int GS, typename PieceFn>
-__device__ __forceinline__ void group_combine(PieceFn piece, int np, int hcnt, __half* out_rows,
-                                              float* out_slot, int* status, float* sm,
-                                              int gtid, int bar_id) {
-  using G = Group<D, GT, GS>;
-  constexpr int OPT = G::OPT;
-  constexpr int U = G::U;
-  const int lane = gtid & 31, gw = gtid >> 5;
-  float* sM = sm;
-  float* sL = sm + GT;
-  float* sRed = sm + 2 * GT;
-  float* sW = sRed + G::NWG * GT;
-  float* sLk = sW + ((size_t)np * GT + 3) / 4 * 4;
-
-  // O values of the first U pieces: they do not depend on the weights, so they are requested
-  // before the maxima are known.
-  float4 v[OPT][U];
-#pragma unroll
-  for (int i = 0; i < OPT; ++i) {
-    const int o = gtid + i * GS;
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      v[i][u] = (u < np) ? __ldcg(reinterpret_cast<const float4*>(piece(u)) + o)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  // Maxima and denominators of every piece, kept in shared memory.
-  float mx[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) mx[h] = neg_inf();
-  for (int k = gtid; k < np; k += GS) {
-    const float4* mk = reinterpret_cast<const float4*>(piece(k) + D * GT);
-#pragma unroll
-    for (int h4 = 0; h4 < GT / 4; ++h4) {
-      const float4 m4 = __ldcg(mk + h4);
-      const float4 l4 = __ldcg(mk + GT / 4 + h4);
-      reinterpret_cast<float4*>(sW + (size_t)k * GT)[h4] = m4;
-      reinterpret_cast<float4*>(sLk + (size_t)k * GT)[h4] = l4;
-      mx[4 * h4 + 0] = fmaxf(mx[4 * h4 + 0], m4.x);
-      mx[4 * h4 + 1] = fmaxf(mx[4 * h4 + 1], m4.y);
-      mx[4 * h4 + 2] = fmaxf(mx[4 * h4 + 2], m4.z);
-      mx[4 * h4 + 3] = fmaxf(mx[4 * h4 + 3], m4.w);
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    const float m = warp_max(mx[h]);
-    if (lane == 0) sRed[gw * GT + h] = m;
-  }
-  group_sync(bar_id, GS);
-  if (gtid < GT) {
-    float m = neg_inf();
-    for (int w = 0; w < G::NWG; ++w) m = fmaxf(m, sRed[w * GT + gtid]);
-    sM[gtid] = m;
-  }
-  group_sync(bar_id, GS);
-  // Weights w_k = 2^(m_k - M) replace the maxima in place (each thread rewrites the entries
-  // it stored above); the denominators are summed with them.
-  float ls[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) ls[h] = 0.f;
-  for (int k = gtid; k < np; k += GS) {
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      const float M = sM[h];
-      const float w = (M == neg_inf()) ? 0.f : ex2(sW[(size_t)k * GT + h] - M);
-      sW[(size_t)k * GT + h] = w;
-      ls[h] += w * sLk[(size_t)k * GT + h];
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    float s = ls[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) sRed[gw * GT + h] = s;
-  }
-  group_sync(bar_id, GS);
-  if (gtid < GT) {
-    float s = 0.f;
-    for (int w = 0; w < G::NWG; ++w) s += sRed[w * GT + gtid];
-    sL[gtid] = s;
-  }
-  group_sync(bar_id, GS);
-
-  // O = sum_k w_k O_k, one float4 (4 heads of one head_dim row) per output.
-  float4 acc[OPT];
-#pragma unroll
-  for (int i = 0; i < OPT; ++i) {
-    const int o = gtid + i * GS;
-    const int h0 = (o % (GT / 4)) * 4;
-    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (u < np) {
-        const float* w = sW + (size_t)u * GT + h0;
-        a4.x += w[0] * v[i][u].x;
-        a4.y += w[1] * v[i][u].y;
-        a4.z += w[2] * v[i][u].z;
-        a4.w += w[3] * v[i][u].w;
-      }
-    }
-    acc[i] = a4;
-  }
-  for (int k0 = U; k0 < np; k0 += U) {
-#pragma unroll
-    for (int i = 0; i < OPT; ++i) {
-      const int o = gtid + i * GS;
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        v[i][u] = (k0 + u < np) ? __ldcg(reinterpret_cast<const float4*>(piece(k0 + u)) + o)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int i = 0; i < OPT; ++i) {
-      const int o = gtid + i * GS;
-      const int h0 = (o % (GT / 4)) * 4;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (k0 + u < np) {
-          const float* w = sW + (size_t)(k0 + u) * GT + h0;
-          acc[i].x += w[0] * v[i][u].x;
-          acc[i].y += w[1] * v[i][u].y;
-          acc[i].z += w[2] * v[i][u].z;
-          acc[i].w += w[3] * v[i][u].w;
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < OPT; ++i) {
-    const int o = gtid + i * GS;
-    const int d = o / (GT / 4);
-    const int h0 = (o % (GT / 4)) * 4;
-    const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
-    if (out_rows != nullptr) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int h = h0 + e;
-        if (h < hcnt) {
-          const float L = sL[h];
-          out_rows[(size_t)h * D + d] = __float2half_rn(L > 0.f ? a4[e] / L : 0.f);
-        }
-      }
-    } else {
-      reinterpret_cast<float4*>(out_slot)[o] = acc[i];
-    }
-  }
-  if (gtid < GT) {
-    if (out_slot != nullptr) {
-      out_slot[D * GT + gtid] = sM[gtid];
-      out_slot[D * GT + GT + gtid] = sL[gtid];
-    } else if (gtid < hcnt && !(sL[gtid] > 0.f)) {
-      flag_error(status, PA_ERR_EMPTY_CONTEXT);
-    }
-  }
-  group_sync(bar_id, GS);  // the scratch is reused by the group's next merge
-}
-
-// ---------------------------------------------------------------------------------------
 // Decode step: the new token's rows in a stage (bulk-copied with the page, rk = K row then V
 // row, 16-bit) are quantised like the cache writes, placed into the staged page at token t of
 // the subpage (the copy brought the slot's previous contents), and stored into the cache at
@@ -642,6 +423,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ int s_pend[WARPS][2][6];
   __shared__ int s_npend[WARPS];
   __shared__ int s_wrow[WARPS][DEPTH];  // decode step: page row whose new token a stage holds
+  __shared__ uint64_t s_mmb[WARPS];     // per-warp barrier of the end-of-launch merges
   extern __shared__ __align__(16) uint8_t dsm_raw[];
 
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
@@ -662,6 +444,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   if (lane == 0) {
 #pragma unroll
     for (int s = 0; s < DEPTH; ++s) mbar_init(&wbar[s], 1);
+    mbar_init(&s_mmb[warp], 1);
     fence_mbar_init();
   }
   if (threadIdx.x == 0) {
@@ -1511,79 +1294,57 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // ---- 5. Merges of the segments whose last piece this CTA's warps finished ------------------
   // The pieces of a recorded merge are visible: the recording arrival acquired them, and the
   // barrier below orders that arrival before every warp's reads.
-  // Segments with few pieces are merged one per warp, in parallel; larger ones by groups of
-  // four warps, side by side, and only a merge too large for a group's scratch by the whole
-  // CTA.
+  // Each merge of up to kStageCap pieces is one warp's: it bulk-copies the pieces into the
+  // (now idle) ring memory and merges them from there, side by side with the CTA's other
+  // merges; merges are packed into the ring memory in a fixed order, in waves when they do not
+  // all fit at once. Only a merge of more pieces than the ring memory holds runs on the whole
+  // CTA, reading the pieces from L2.
   if (lane == 0) s_npend[warp] = npend;
-  __syncthreads();  // every warp is past its page loop: the ring memory is free scratch
+  __syncthreads();  // every warp is past its page loop: the ring memory is free
+  constexpr size_t kRing = (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST);
+  constexpr int kStageCap = (int)(kRing / (SLOT * sizeof(float)));
   float* scratch = reinterpret_cast<float*>(k_tiles);
-  // Merges of up to kWarpMergeMax pieces run one per warp in parallel, larger ones in the
-  // groups of four warps. 16-row head tiles keep more registers per piece and never merge in
-  // a single warp.
-  // Pieces per step of a one-warp merge: four where the launch leaves 255 registers a thread
-  // (8 warps), two under the 168 of 12-warp launches.
-  constexpr int kWarpStep = (WARPS <= 8) ? 4 : 2;
-  constexpr int kWarpMerge = (GT != 8) ? 0 : kWarpMergeMax;
-  int idx = 0;
-  for (int w = 0; w < WARPS; ++w) {
-    for (int e = 0; e < s_npend[w]; ++e) {
-      const int* pe = s_pend[w][e];
-      const int np = pe[2];
-      if (np > kWarpMerge) continue;
-      if ((idx++ % WARPS) != warp) continue;
-      const int segid = pe[0], wf = pe[1], b = pe[3], hbase = pe[4], hcnt = pe[5];
-      auto piece = [&](int k) -> const float* {
-        return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
-      };
-      if (a.mode == kModeStream) {
-        warp_combine<D, GT, kWarpStep>(piece, np, lane, hcnt,
-                                       a.out + ((size_t)b * a.H + hbase) * D, nullptr, a.status);
-      } else {
-        warp_combine<D, GT, kWarpStep>(piece, np, lane, hcnt, nullptr,
-                                       a.part_out + (size_t)segid * SLOT, a.status);
-      }
-      if (lane == 0) a.counters[segid] = 0;
-    }
-  }
-  constexpr int GS = 128;
-  constexpr int NG = NTHR / GS;
-  constexpr size_t kGroupBytes = (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST) / NG / 16 * 16;
-  const int grp = warp / (GS / 32);
-  int idx_g = 0;
+  const bool stream = (a.mode == kModeStream);
+  int used = 0, inwave = 0;
+  uint32_t mph = 0;  // phase parity of this warp's merge barrier
   bool any_big = false;
   for (int w = 0; w < WARPS; ++w) {
     for (int e = 0; e < s_npend[w]; ++e) {
       const int* pe = s_pend[w][e];
       const int np = pe[2];
-      if (np <= kWarpMerge) continue;
-      if (Group<D, GT, GS>::floats(np) * sizeof(float) > kGroupBytes) {
+      if (np > kStageCap) {
         any_big = true;
         continue;
       }
-      if ((idx_g++ % NG) != grp) continue;
-      const int segid = pe[0], wf = pe[1], b = pe[3], hbase = pe[4], hcnt = pe[5];
-      auto piece = [&](int k) -> const float* {
-        return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
-      };
-      const bool stream = (a.mode == kModeStream);
-      group_combine<D, GT, GS>(piece, np, hcnt,
-                               stream ? a.out + ((size_t)b * a.H + hbase) * D : nullptr,
-                               stream ? nullptr : a.part_out + (size_t)segid * SLOT, a.status,
-                               reinterpret_cast<float*>(k_tiles + grp * kGroupBytes),
-                               (int)threadIdx.x - grp * GS, 1 + grp);
-      if ((int)threadIdx.x == grp * GS) a.counters[segid] = 0;
+      if (used + np > kStageCap || inwave == WARPS) {
+        __syncthreads();  // the wave's merges are done with the ring memory
+        used = 0;
+        inwave = 0;
+      }
+      if (inwave == warp) {
+        const int segid = pe[0], wf = pe[1], b = pe[3], hbase = pe[4], hcnt = pe[5];
+        if (!staged_combine<D, GT>(a.part, wf, np, lane, hcnt,
+                                   stream ? a.out + ((size_t)b * a.H + hbase) * D : nullptr,
+                                   stream ? nullptr : a.part_out + (size_t)segid * SLOT,
+                                   a.status, scratch + (size_t)used * SLOT, &s_mmb[warp], mph)) {
+          // Timed out: let the copies land before the memory is used again.
+          (void)mbar_wait_bounded(&s_mmb[warp], mph, nullptr);
+        }
+        mph ^= 1u;
+        if (lane == 0) a.counters[segid] = 0;
+      }
+      used += np;
+      ++inwave;
     }
   }
   if (!any_big) return;
-  __syncthreads();  // the groups are done with their parts of the scratch
+  __syncthreads();  // the staged merges are done with the ring memory
   for (int w = 0; w < WARPS; ++w) {
     for (int e = 0; e < s_npend[w]; ++e) {
       const int* pe = s_pend[w][e];
       const int segid = pe[0], wf = pe[1], np = pe[2], b = pe[3], hbase = pe[4], hcnt = pe[5];
-      if (np <= kWarpMerge) continue;
-      if (Group<D, GT, GS>::floats(np) * sizeof(float) <= kGroupBytes) continue;
-      if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) >
-          (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST)) {
+      if (np <= kStageCap) continue;
+      if (Coop<D, GT, NTHR, 8>::floats(np) * sizeof(float) > kRing) {
         if (threadIdx.x == 0) {
           flag_error(a.status, PA_ERR_WORKSPACE);
           a.counters[segid] = 0;  // leave the counter ready for the next call
@@ -1593,7 +1354,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       auto piece = [&](int k) -> const float* {
         return a.part + ((size_t)(wf + k) * 2 + (k == 0 ? 1 : 0)) * SLOT;
       };
-      if (a.mode == kModeStream) {
+      if (stream) {
         coop_combine<D, GT, NTHR, 8>(piece, np, hcnt, a.out + ((size_t)b * a.H + hbase) * D,
                                      nullptr, a.status, scratch);
       } else {
