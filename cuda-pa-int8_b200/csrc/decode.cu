@@ -424,6 +424,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ int s_npend[WARPS];
   __shared__ int s_wrow[WARPS][DEPTH];  // decode step: page row whose new token a stage holds
   __shared__ uint64_t s_mmb[WARPS];     // per-warp barrier of the end-of-launch merges
+  __shared__ int s_nblk[WARPS][32];     // block ids of a warp's next batch of pages
+  __shared__ int s_nmeta[WARPS][32];    // their (kv_head << 3) | subpage
+  __shared__ int s_nwr[WARPS][32];      // their decode-step new-token sequence, or -1
   extern __shared__ __align__(16) uint8_t dsm_raw[];
 
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
@@ -581,7 +584,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   const int n = (int)(p1 - p0);
-  int npend = 0;  // segments whose merge this warp owes (it arrived last)
+  int nrec = 0;              // shared segments whose arrival this warp recorded
+  int old0 = 0, old1 = 0;    // lane 0: the arrival counters' values before those arrivals
   if (n > 0) {
 
   // ---- 3. Consumer position and the first piece's q rows --------------------------------------
@@ -645,6 +649,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int e2 = amax > 0.f ? ((__float_as_int(amax) >> 23) & 0xff) - 126 : 6;
     qsc = __int_as_float((127 + e2 - 6) << 23);
     const float inv = __int_as_float((127 + 6 - e2) << 23);
+    // Rounding to the nearest integer (ties to even) by adding and subtracting 1.5 * 2^23:
+    // exact for |x| < 2^22 (here |x| <= 64), two full-rate adds instead of the conversion
+    // pipe, which all warps of an SM need at once when a launch starts. The sum's low byte is
+    // the int8 two's-complement byte of the rounded value.
+    constexpr float kRound = 12582912.f;
 #pragma unroll
     for (int si = 0; si < NS; ++si) {
       const uint32_t w4[4] = {src[si].x, src[si].y, src[si].z, src[si].w};
@@ -656,13 +665,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const float t = tt[h];
-          const float p1 = rintf(t);
-          const float r1 = (t - p1) * 128.f;
-          const float p2 = rintf(r1);
-          const float p3 = rintf((r1 - p2) * 128.f);
-          q1[2 * e + h] = (int)p1;
-          q2[2 * e + h] = (int)p2;
-          q3[2 * e + h] = (int)p3;
+          const float s1 = __fadd_rn(t, kRound);
+          const float r1 = (t - __fsub_rn(s1, kRound)) * 128.f;
+          const float s2 = __fadd_rn(r1, kRound);
+          const float s3 = __fadd_rn((r1 - __fsub_rn(s2, kRound)) * 128.f, kRound);
+          q1[2 * e + h] = __float_as_int(s1);
+          q2[2 * e + h] = __float_as_int(s2);
+          q3[2 * e + h] = __float_as_int(s3);
         }
       }
       dst[si] = make_uint4(pack_s8x4(q1[0], q1[1], q1[2], q1[3]),
@@ -705,38 +714,59 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // With a decode step, wr receives the sequence whose new token lies in the page (the last
   // page of a segment whose context and block id are valid), else -1.
   const bool step_write = a.new_k != nullptr;
-  auto batch_info = [&](int jbase, int& wr) {
-    int pk = 0;
+  // Page jbase + lane of the range: the address of its block id, its (kv_head << 3) | subpage
+  // and, for a decode step, the sequence whose new token it holds (else -1).
+  auto page_ref = [&](int jbase, int& meta, int& wr) -> const int* {
+    meta = 0;
     wr = -1;
-    const int j = jbase + lane;
-    if (j < n) {
-      int b, seg, sp;
-      locate((int)(p0 + j), b, seg, sp);
-      const int kvh = seg / a.HT;
-      const int bi = sp / a.subs;
-      const int sub = sp - bi * a.subs;
-      int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + bi);
-      bool ok = true;
-      if (blk < 0 || blk >= a.NB) {
-        flag_error(a.status, PA_ERR_BLOCK_ID);
-        blk = 0;
-        ok = false;
-      }
-      pk = ((blk * a.KVH + kvh) << 3) | sub;
-      if (step_write && ok && sp == pages_of(b) - 1 && !((s_over[b >> 5] >> (b & 31)) & 1u))
-        wr = b;
-    }
-    return pk;
+    const int jj = jbase + lane;
+    if (jj >= n) return nullptr;
+    int b, seg, sp;
+    locate((int)(p0 + jj), b, seg, sp);
+    const int bi = sp / a.subs;
+    meta = ((seg / a.HT) << 3) | (sp - bi * a.subs);
+    if (step_write && sp == pages_of(b) - 1 && !((s_over[b >> 5] >> (b & 31)) & 1u)) wr = b;
+    return a.block_table + (size_t)b * a.max_blocks + bi;
   };
-  int curw = -1, nxtw = -1;
-  int cur = batch_info(0, curw);
-  int nxt = 0;  // block ids of pages 32..63: read once the first copies are on their way
+  // Copy descriptor (row << 3) | subpage; a block id outside the cache is flagged and read as
+  // block 0, and its new token (if any) is not written.
+  auto pack_page = [&](int blk, int meta, int& wr) -> int {
+    if (blk < 0 || blk >= a.NB) {
+      flag_error(a.status, PA_ERR_BLOCK_ID);
+      blk = 0;
+      wr = -1;
+    }
+    return ((blk * a.KVH + (meta >> 3)) << 3) | (meta & 7);
+  };
+  // The block ids of the next 32 pages are copied into shared memory in the background
+  // (cp.async) a batch ahead, so no block-table load ever stalls the page loop.
+  auto prefetch_batch = [&](int jbase) {
+    int meta, wr;
+    const int* p = page_ref(jbase, meta, wr);
+    s_nmeta[warp][lane] = meta;
+    s_nwr[warp][lane] = wr;
+    if (p != nullptr) {
+      cp_async_4(&s_nblk[warp][lane], p);
+    } else {
+      s_nblk[warp][lane] = 0;
+    }
+    cp_async_commit();
+  };
+  auto take_batch = [&](int& wr) -> int {
+    cp_async_wait_all();
+    wr = s_nwr[warp][lane];
+    return pack_page(s_nblk[warp][lane], s_nmeta[warp][lane], wr);
+  };
+  int curw, meta0;
+  const int* bref0 = page_ref(0, meta0, curw);
+  const int blk0 = bref0 != nullptr ? __ldg(bref0) : 0;
+  prefetch_batch(32);  // requested before the first batch's ids are waited for
+  int cur = pack_page(blk0, meta0, curw);
 
   auto issue = [&](int j, int s) {
     if (j > 0 && (j & 31) == 0) {
-      cur = nxt;
-      curw = nxtw;
-      nxt = batch_info(j + 32, nxtw);
+      cur = take_batch(curw);
+      prefetch_batch(j + 32);
     }
     const int pk = __shfl_sync(0xffffffffu, cur, j & 31);
     // Decode step: the page holding sequence wb's new token also brings the token's K and V
@@ -787,7 +817,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __syncwarp();
   for (int j = 0; j < npro; ++j) issue(j, j);
   int issued = npro;
-  nxt = batch_info(32, nxtw);
   convert_q();
 
   // Shared-memory offsets of the K cells this lane reads (chunk of load si, token of n-tile
@@ -843,6 +872,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       convert_q();
       q_b = cb;
       q_seg = cseg;
+    }
+    // When this piece ends its segment and the range goes on, the next segment's q rows are
+    // brought into L1 while this piece runs, so the next piece's q fetch does not wait on L2.
+    if (csp + len == cpg && j + len < n) {
+      int nb = cb, ns = cseg + 1;
+      if (ns == SEGS) {
+        ns = 0;
+        do { ++nb; } while (pages_of(nb) == 0);
+      }
+      const int kvh = ns / a.HT;
+      const int hl = (ns - kvh * a.HT) * GT + (lane >> 1);
+      if (lane < 2 * GT && hl < a.G)
+        prefetch_l1(a.q + ((size_t)nb * a.H + (size_t)kvh * a.G + hl) * D + (lane & 1) * (D / 2));
     }
     m0 = neg_inf();
     l0 = 0.f;
@@ -1245,19 +1287,23 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         // A piece of a segment shared with neighbouring warps.
         write_slot(a.part + ((size_t)wg * 2 + (piece_sp0 == 0 ? 1 : 0)) * SLOT);
         __syncwarp();
-        int old = 0;
-        // Release this piece; the arrival that completes the count acquires all of them.
-        if (lane == 0) old = atom_add_acq_rel_gpu(a.counters + segid, 1);
-        old = __shfl_sync(0xffffffffu, old, 0);
         const long long s_start = (long long)s_pre[cb] + (long long)cseg * cpg;
         const long long s_end = s_start + cpg;
         const int wf = (int)(((s_start + 1) * Wt - 1) / T);
         const int wl = (int)((s_end * Wt - 1) / T);
         const int np = wl - wf + 1;
-        if (old == np - 1 && lane == 0) {
-          // Last arrival: merge after the page loop, when its registers are free. A warp
-          // finishes at most two split segments (its first and its last).
-          int* pe = s_pend[warp][npend];
+        // Release this piece; the arrival that completes the count acquires all of them and
+        // owes the merge, which runs after the page loop, when the registers are free. The
+        // merge is recorded now and kept if the atomic's old value shows the last arrival;
+        // that value is first read after the loop, so the loop does not wait for the atomic.
+        // A warp shares at most two segments (its first and its last).
+        if (lane == 0 && nrec < 2) {
+          if (nrec == 0) {
+            old0 = atom_add_acq_rel_gpu(a.counters + segid, 1);
+          } else {
+            old1 = atom_add_acq_rel_gpu(a.counters + segid, 1);
+          }
+          int* pe = s_pend[warp][nrec];
           pe[0] = segid;
           pe[1] = wf;
           pe[2] = np;
@@ -1265,7 +1311,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           pe[4] = hbase;
           pe[5] = hcnt;
         }
-        npend += (old == np - 1) ? 1 : 0;
+        ++nrec;
       }
     }
 
@@ -1299,7 +1345,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // merges; merges are packed into the ring memory in a fixed order, in waves when they do not
   // all fit at once. Only a merge of more pieces than the ring memory holds runs on the whole
   // CTA, reading the pieces from L2.
-  if (lane == 0) s_npend[warp] = npend;
+  if (lane == 0) {
+    // The recorded merges this warp owes: those whose arrival completed the count.
+    int k = 0;
+    for (int e = 0; e < min(nrec, 2); ++e) {
+      const int* pe = s_pend[warp][e];
+      if ((e == 0 ? old0 : old1) == pe[2] - 1) {
+        if (k != e)
+          for (int f = 0; f < 6; ++f) s_pend[warp][k][f] = pe[f];
+        ++k;
+      }
+    }
+    s_npend[warp] = k;
+  }
   __syncthreads();  // every warp is past its page loop: the ring memory is free
   constexpr size_t kRing = (size_t)WARPS * DEPTH * (C::KT + C::VT + C::ST);
   constexpr int kStageCap = (int)(kRing / (SLOT * sizeof(float)));
@@ -1432,7 +1490,7 @@ cudaError_t launch_one(const DecodeArgs& a, const CUtensorMap* maps, int grid,
   constexpr int W = Shape<KVK, GT>::W;
   constexpr int DP = Shape<KVK, GT>::DP;
   using C = Tile<KVK, 128, GT, DP, W>;
-  static_assert(C::SMEM_STEP + 9 * 1024 <= 227 * 1024, "shared memory of a step launch");
+  static_assert(C::SMEM_STEP + 14 * 1024 <= 227 * 1024, "shared memory of a step launch");
   auto kern = decode_kernel<KVK, 128, GT, DP, W>;
   // The shared-memory opt-in is a per-device function attribute: set it once per device, to
   // the larger size of a decode step launch.
