@@ -55,6 +55,24 @@ __device__ __forceinline__ int8_t quant1(float x, float s) {
   return (int8_t)q;
 }
 
+// quant1(x, s) without the division where that is provably the same: inv = 1/s rounded to
+// nearest, y = x * inv rounded to nearest, so |y - x/s| <= 2^-23 |x/s| < 2^-15 for
+// |y| < 256. When y is farther than 2^-14 from a half-integer, x/s rounds to the same integer
+// as y, which the 1.5 * 2^23 add-and-subtract rounding gives (ties to even, exact for
+// |y| < 2^22); the sum's low bits hold that integer. Everything else (values near a
+// half-integer, s = 0 or non-finite, |y| >= 256) takes the division.
+__device__ __forceinline__ int quant_fast(float x, float s, float inv) {
+  constexpr float kRound = 12582912.f;
+  const float y = __fmul_rn(x, inv);
+  const float s1 = __fadd_rn(y, kRound);
+  const float d = __fsub_rn(y, __fsub_rn(s1, kRound));
+  if (fabsf(d) < 0.5f - 0x1p-14f && fabsf(y) < 256.f) {  // false for NaN
+    const int q = __float_as_int(s1) - 0x4B400000;
+    return q < -127 ? -127 : (q > 127 ? 127 : q);
+  }
+  return quant1(x, s);
+}
+
 // Load DPL consecutive input values starting at src (src aligned to DPL elements).
 template <typename T, int DPL>
 __device__ __forceinline__ void load_vals(const T* src, float (&x)[DPL]) {
@@ -102,8 +120,9 @@ __device__ __forceinline__ RowQ<KIND, D> warp_quantize_row(const T* src, int lan
     }
     uint8_t qv[DPL];
     if constexpr (KIND == kRowsI8) {
+      const float inv = __frcp_rn(s);
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) qv[e] = (uint8_t)quant1(x[e], s);
+      for (int e = 0; e < DPL; ++e) qv[e] = (uint8_t)quant_fast(x[e], s, inv);
     } else {
 #pragma unroll
       for (int e = 0; e < DPL; ++e)

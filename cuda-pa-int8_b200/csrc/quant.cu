@@ -76,12 +76,18 @@ __global__ void __launch_bounds__(256) step_rows_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
-// Block-granular prefill: one CTA per (block j, kv-head, sequence). The block's K and V rows
-// are loaded with one vector load per lane and row, several rows in flight per warp, quantised
-// (or rounded) into shared memory, and written as whole K and V pages with 16-byte stores,
-// then the scales. Tokens past the context are written as zeros with scale 0.
+// Block-granular prefill: one warp per (sequence, block, kv-head, K|V) page, 16 tokens at a
+// time. A lane holds four consecutive head_dim values of each of the 16 rows (one vector load
+// per row, all in flight together), the warp reduces the 16 row maxima together, and the lane
+// writes the quantised (or fp16) values straight into the page layout with 16-byte stores:
+//   K page [D/8][bs][8]: the lane pair (2c, 2c+1) owns 8-wide chunk c; after the pair swaps
+//     half of its words, lane 2c writes the group's tokens 0-7 and lane 2c+1 tokens 8-15;
+//   V page [D][bs]: lane l owns head_dim rows 4l..4l+3, 16 consecutive tokens each.
+// No shared memory and no per-element index arithmetic. Tokens past the context are written
+// as zeros with scale 0.
 // ---------------------------------------------------------------------------------------
 constexpr int kPrefillThreads = 256;
+constexpr int kPrefillBlocksPerCta = kPrefillThreads / 64;  // a K warp and a V warp per block
 
 // The four consecutive input values of one lane (8 bytes for 16-bit inputs, 16 for fp32).
 __device__ __forceinline__ void load4(const __half* p, float (&x)[4]) {
@@ -101,132 +107,153 @@ __device__ __forceinline__ void load4(const float* p, float (&x)[4]) {
   x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
 }
 
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 template <typename T, bool I8, int D>
-__global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
+__global__ void __launch_bounds__(kPrefillThreads, 2) prefill_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int L, int KVH,
     const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
     void* __restrict__ k_cache, void* __restrict__ v_cache, float* __restrict__ k_scales,
     float* __restrict__ v_scales, int NB, int bs, const float* __restrict__ kfix,
     const float* __restrict__ vfix, int* status) {
-  static_assert(D == 128, "a lane loads four consecutive head_dim values");
-  using OutT = typename std::conditional<I8, int8_t, __half>::type;
-  constexpr int ELEM = sizeof(OutT);
-  constexpr int NW = kPrefillThreads / 32;
-  constexpr int RB = 4;  // rows per warp whose loads are in flight together
-  extern __shared__ __align__(16) uint8_t sm[];
-  OutT* kq = reinterpret_cast<OutT*>(sm);                              // [bs][D]
-  OutT* vq = kq + (size_t)bs * D;                                      // [bs][D]
-  float* ksm = reinterpret_cast<float*>(sm + 2 * (size_t)bs * D * ELEM);  // [bs]
-  float* vsm = ksm + bs;                                               // [bs]
-
-  const int j = blockIdx.x;
+  static_assert(D == 128, "a lane holds four consecutive head_dim values");
+  constexpr unsigned kAll = 0xffffffffu;
+  constexpr int ELEM = I8 ? 1 : 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x * kPrefillBlocksPerCta + (warp >> 1);
+  const bool is_v = (warp & 1) != 0;
   const int kvh = blockIdx.y;
   const int b = blockIdx.z;
   int ctx = __ldg(context_lens + b);
   const int cap = min(L, max_blocks * bs);
   if (ctx > cap) {
-    if (threadIdx.x == 0 && j == 0 && kvh == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
+    if (threadIdx.x == 0 && blockIdx.x == 0 && kvh == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
     ctx = cap;
   }
   if (ctx < 0) ctx = 0;
-  const int nblk = (ctx + bs - 1) / bs;
-  if (j >= nblk) return;
+  if (j >= (ctx + bs - 1) / bs) return;  // warp-uniform
   const int blk = __ldg(block_table + (size_t)b * max_blocks + j);
   if (blk < 0 || blk >= NB) {
-    if (threadIdx.x == 0) flag_error(status, PA_ERR_BLOCK_ID);
+    if (lane == 0 && !is_v) flag_error(status, PA_ERR_BLOCK_ID);
     return;
   }
-  const int t0 = j * bs;
-  const int valid = min(bs, ctx - t0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t page = (size_t)blk * KVH + kvh;
+  const size_t tstride = (size_t)KVH * D;
+  const T* src = (is_v ? v : k) + ((size_t)b * L * KVH + kvh) * D + lane * 4;
+  uint8_t* pg = reinterpret_cast<uint8_t*>(is_v ? v_cache : k_cache) + page * (size_t)D * bs * ELEM;
+  float* scl = (is_v ? v_scales : k_scales) + page * bs;
+  const float* fix = is_v ? vfix : kfix;
+  const int c = lane >> 1;       // K: the lane pair's 8-wide chunk
+  const int hlf = lane & 1;      // K: which half of the chunk the lane holds
 
-  // Rows 0 .. bs-1 are K rows, bs .. 2bs-1 V rows; warp w takes rows w, w + NW, ...
-  for (int r0 = warp; r0 < 2 * bs; r0 += NW * RB) {
-    float x[RB][4];
+  for (int g0 = 0; g0 < bs; g0 += 16) {
+    const int valid = min(16, ctx - (j * bs + g0));  // rows of this group inside the context
+    float x[16][4];
 #pragma unroll
-    for (int rb = 0; rb < RB; ++rb) {
-      const int r = r0 + rb * NW;
-      const int i = r < bs ? r : r - bs;
-      if (r < 2 * bs && i < valid) {
-        load4((r < bs ? k : v) + (((size_t)b * L + t0 + i) * KVH + kvh) * D + lane * 4, x[rb]);
+    for (int t = 0; t < 16; ++t) {
+      if (t < valid) {
+        load4(src + (size_t)(j * bs + g0 + t) * tstride, x[t]);
       } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) x[rb][e] = 0.f;
+        for (int e = 0; e < 4; ++e) x[t][e] = 0.f;
       }
     }
+    constexpr int KW = I8 ? 1 : 2;  // words of a lane's four values: int8 one, fp16 two
+    // Per token, the lane's four values as stored: int8 bytes (zero past the context) or fp16.
+    uint32_t kw[16][KW];
+    if constexpr (I8) {
+      // Row maxima, reduced together: after the steps over lane masks 16, 8, 4, 2 lane l holds
+      // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it.
+      float m[16];
 #pragma unroll
-    for (int rb = 0; rb < RB; ++rb) {
-      const int r = r0 + rb * NW;
-      if (r >= 2 * bs) break;  // uniform across the warp
-      const bool is_v = r >= bs;
-      const int i = is_v ? r - bs : r;
-      OutT* q = (is_v ? vq : kq) + (size_t)i * D + lane * 4;
-      if constexpr (I8) {
-        const float* fix = is_v ? vfix : kfix;
-        float s;
-        if (i >= valid) {
-          s = 0.f;
-        } else if (fix != nullptr) {
-          s = __ldg(fix);
+      for (int t = 0; t < 16; ++t)
+        m[t] = fmaxf(fmaxf(fabsf(x[t][0]), fabsf(x[t][1])), fmaxf(fabsf(x[t][2]), fabsf(x[t][3])));
+#pragma unroll
+      for (int h = 8, msk = 16; h >= 1; h >>= 1, msk >>= 1) {
+        const bool up = (lane & msk) != 0;
+#pragma unroll
+        for (int i = 0; i < h; ++i) {
+          const float send = up ? m[i] : m[i + h];
+          const float keep = up ? m[i + h] : m[i];
+          m[i] = fmaxf(keep, __shfl_xor_sync(kAll, send, msk));
+        }
+      }
+      const float am = fmaxf(m[0], __shfl_xor_sync(kAll, m[0], 1));
+      const int row = lane >> 1;
+      float s = 0.f;
+      if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
+      const float inv = __frcp_rn(s);
+      if (hlf == 0) scl[g0 + row] = s;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const float st = __shfl_sync(kAll, s, 2 * t);
+        const float it = __shfl_sync(kAll, inv, 2 * t);
+        uint32_t w = 0u;
+        if (t < valid) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) w |= (uint32_t)(quant_fast(x[t][e], st, it) & 0xff) << (8 * e);
+        }
+        kw[t][0] = w;
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        kw[t][0] = half2_bits(x[t][0], x[t][1]);
+        kw[t][1] = half2_bits(x[t][2], x[t][3]);
+      }
+    }
+    if (!is_v) {
+      // The pair swaps half of its words: lane 2c keeps tokens 0-7 and receives its partner's
+      // words for them, lane 2c+1 the same for tokens 8-15.
+      uint32_t pw[8][KW];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int w = 0; w < KW; ++w)
+          pw[i][w] = __shfl_xor_sync(kAll, hlf ? kw[i][w] : kw[8 + i][w], 1);
+      uint8_t* dst = pg + ((size_t)c * bs + g0 + 8 * hlf) * 8 * ELEM;
+#pragma unroll
+      for (int i = 0; i < 8; i += (I8 ? 2 : 1)) {
+        if constexpr (I8) {
+          // Two tokens of 8 bytes: lane 2c's half of the chunk, then lane 2c+1's.
+          const uint32_t a0 = hlf ? pw[i][0] : kw[i][0], a1 = hlf ? kw[8 + i][0] : pw[i][0];
+          const uint32_t b0 = hlf ? pw[i + 1][0] : kw[i + 1][0];
+          const uint32_t b1 = hlf ? kw[9 + i][0] : pw[i + 1][0];
+          *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(a0, a1, b0, b1);
         } else {
-          float am = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(x[rb][e]));
-          am = warp_max(am);
-          s = token_scale<T>(am);
-        }
-        int8_t qv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) qv[e] = (i < valid) ? quant1(x[rb][e], s) : (int8_t)0;
-        *reinterpret_cast<uint32_t*>(q) = *reinterpret_cast<const uint32_t*>(qv);
-        if (lane == 0) (is_v ? vsm : ksm)[i] = s;
-      } else {
-        const __half2 h0 = __floats2half2_rn(x[rb][0], x[rb][1]);
-        const __half2 h1 = __floats2half2_rn(x[rb][2], x[rb][3]);
-        *reinterpret_cast<uint2*>(q) = make_uint2(*reinterpret_cast<const uint32_t*>(&h0),
-                                                  *reinterpret_cast<const uint32_t*>(&h1));
-      }
-    }
-  }
-  __syncthreads();
-
-  constexpr int PER16 = 16 / ELEM;  // elements per 16-byte store
-  const int units = D * bs / PER16;
-  for (int which = 0; which < 2; ++which) {
-    const OutT* q_sm = which ? vq : kq;
-    OutT* pg = reinterpret_cast<OutT*>(which ? v_cache : k_cache) + page * (size_t)D * bs;
-    for (int u = threadIdx.x; u < units; u += blockDim.x) {
-      alignas(16) OutT tmp[PER16];
-      const int e0 = u * PER16;  // element offset inside the page
-      if (which == 0) {
-        // K page [D/8][bs][8]: element e0 -> chunk c, token t, lane-in-chunk w
-#pragma unroll
-        for (int e = 0; e < PER16; ++e) {
-          const int el = e0 + e;
-          const int c = el / (bs * 8);
-          const int rem = el - c * bs * 8;
-          const int t = rem >> 3;
-          const int w = rem & 7;
-          tmp[e] = q_sm[t * D + c * 8 + w];
-        }
-      } else {
-        // V page [D][bs]
-#pragma unroll
-        for (int e = 0; e < PER16; ++e) {
-          const int el = e0 + e;
-          const int d = el / bs;
-          const int t = el - d * bs;
-          tmp[e] = q_sm[t * D + d];
+          // One token of 16 bytes.
+          const uint32_t l0 = hlf ? pw[i][0] : kw[i][0], l1 = hlf ? pw[i][1] : kw[i][1];
+          const uint32_t h0 = hlf ? kw[8 + i][0] : pw[i][0], h1 = hlf ? kw[8 + i][1] : pw[i][1];
+          *reinterpret_cast<uint4*>(dst + i * 16) = make_uint4(l0, l1, h0, h1);
         }
       }
-      *reinterpret_cast<uint4*>(pg + e0) = *reinterpret_cast<const uint4*>(tmp);
-    }
-  }
-  if constexpr (I8) {
-    for (int t = threadIdx.x; t < 2 * bs; t += blockDim.x) {
-      if (t < bs) k_scales[page * bs + t] = ksm[t];
-      else v_scales[page * bs + t - bs] = vsm[t - bs];
+    } else {
+      // Per head_dim row 4 * lane + e, the group's 16 tokens: byte (int8) or half (fp16) e of
+      // every token's word.
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint32_t vw[4 * KW];
+#pragma unroll
+        for (int u = 0; u < 4 * KW; ++u) {
+          if constexpr (I8) {
+            const uint32_t sel = (uint32_t)e | ((uint32_t)(4 + e) << 4);
+            vw[u] = __byte_perm(__byte_perm(kw[4 * u][0], kw[4 * u + 1][0], sel),
+                                __byte_perm(kw[4 * u + 2][0], kw[4 * u + 3][0], sel), 0x5410);
+          } else {
+            // Halves e of tokens 2u and 2u + 1.
+            const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+            vw[u] = __byte_perm(kw[2 * u][e >> 1], kw[2 * u + 1][e >> 1], sel);
+          }
+        }
+        uint8_t* dst = pg + ((size_t)(4 * lane + e) * bs + g0) * ELEM;
+#pragma unroll
+        for (int u = 0; u < KW; ++u)
+          *reinterpret_cast<uint4*>(dst + 16 * u) =
+              make_uint4(vw[4 * u], vw[4 * u + 1], vw[4 * u + 2], vw[4 * u + 3]);
+      }
     }
   }
 }
@@ -313,19 +340,12 @@ cudaError_t launch_prefill_t(bool i8, const void* k, const void* v, int S, int L
                              float* ks, float* vs, int NB, int bs, const float* kf,
                              const float* vf, int* status, cudaStream_t st) {
   if (S == 0 || max_blocks == 0) return cudaSuccess;
-  const dim3 grid(max_blocks, KVH, S);
+  const dim3 grid((max_blocks + kPrefillBlocksPerCta - 1) / kPrefillBlocksPerCta, KVH, S);
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
-  // Shared memory: the quantised K and V rows of one block plus their scales.
-  const size_t smem = 2 * (size_t)bs * 128 * (i8 ? 1 : 2) + 2 * (size_t)bs * 4;
   auto kern = i8 ? prefill_kernel<T, true, 128> : prefill_kernel<T, false, 128>;
-  if (smem > 48 * 1024) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  kern<<<grid, kPrefillThreads, smem, st>>>(kk, vv, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs,
-                                            NB, bs, kf, vf, status);
+  kern<<<grid, kPrefillThreads, 0, st>>>(kk, vv, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs, NB,
+                                         bs, kf, vf, status);
   return cudaGetLastError();
 }
 

@@ -256,3 +256,49 @@ def test_int8_cache_smaller_than_fp16():
     fp16 = PagedKVCache(variant="fp16", **kw).kv_bytes()
     int8 = PagedKVCache(variant="int8_per_token", **kw).kv_bytes()
     assert int8 / fp16 < 0.6
+
+
+def _near_half_integers(rng, shape, s):
+    """fp16 values whose quotient by s lies on a half-integer (as rounded to fp16) or one or
+    two fp16 ulps beside it, over the whole int8 range and a little past it."""
+    x = ((rng.integers(-130, 130, size=shape) + 0.5) * float(s)).astype(np.float16)
+    steps = rng.integers(-2, 3, size=shape).astype(np.int16)
+    return (x.view(np.int16) + steps).view(np.float16)
+
+
+@pytest.mark.parametrize("scale", [0.37, 0.021, 1.0 / 3.0, 7.77e-3, 0.5, 1.7e-5])
+def test_quantizer_near_half_integers_bit_exact(scale):
+    """The write kernels quantise by a reciprocal multiply where that provably rounds like the
+    division, and divide elsewhere. Values placed on and beside the half-integer boundaries of
+    fixed scales, through the token writes and the prefill scatter: bit-exact with the
+    oracle's division."""
+    s = np.float32(scale)
+    rng = np.random.default_rng(int(scale * 1e7) + 1)
+    KVH, L = 2, 48
+    k = _near_half_integers(rng, (2, L, KVH, 128), s)
+    v = _near_half_integers(rng, (2, L, KVH, 128), s)
+    ts = torch.tensor(s, device="cuda")
+    # Token writes.
+    rows_k, rows_v = k.reshape(-1, KVH, 128), v.reshape(-1, KVH, 128)
+    slots = np.arange(rows_k.shape[0], dtype=np.int32)
+    nb = rows_k.shape[0] // 16
+    kc, vc, ks, vs = _caches(nb, KVH)
+    tk, tv = to_cuda(rows_k, rows_v)
+    _ops().quantize_into_cache(tk, tv, kc, vc, ks, vs, torch.from_numpy(slots).cuda(), 16,
+                               k_scale=ts, v_scale=ts)
+    okc, ovc, oks, ovs = _oracle_rows(rows_k, rows_v, slots, nb, KVH, 16, "f16", s, s)
+    assert _bits_equal(kc, okc) and _bits_equal(vc, ovc)
+    # Prefill scatter of the same rows (two sequences of 48 and 37 tokens).
+    cl = np.array([L, 37], np.int32)
+    bt = np.random.default_rng(3).permutation(8).astype(np.int32).reshape(2, 4)
+    kc, vc, ks, vs = _caches(8, KVH)
+    tk, tv, tbt, tcl = to_cuda(k, v, bt, cl)
+    _ops().prefill_into_cache(tk, tv, kc, vc, tbt, tcl, 16, k_scales=ks, v_scales=vs,
+                              k_scale=ts, v_scale=ts)
+    kq = pa_oracle.quantize_with_scale(k.astype(np.float32), s)
+    vq = pa_oracle.quantize_with_scale(v.astype(np.float32), s)
+    okc, ovc = pa_oracle.scatter_paged_cache(kq, vq, cl, bt, 8, 16)
+    assert np.array_equal(kc.cpu().numpy().view(np.uint8), okc.view(np.uint8))
+    assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
+    sc = np.full((2, L, KVH), s, np.float32)
+    assert _bits_equal(ks, pa_oracle.scatter_scales(sc, cl, bt, 8, KVH, 16))

@@ -310,3 +310,4 @@ def test_decode_plan_matches_decode_and_rejects_other_shapes():
             plan.run(q=q2[:1].contiguous())
         with pytest.raises(RuntimeError, match="context_lens must be >= 1"):
             plan.run(host_context_lens=torch.zeros_like(c["cl"].cpu()))
+
