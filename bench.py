@@ -336,14 +336,16 @@ def make_step(w, splitk=False, validate=False, decode_only=False):
         dec_launches = 2 if use_split else 1
 
     if w.step_tokens and not decode_only:
-        # The decode step API: the new token of every sequence is written into the cache by
-        # the decode kernel itself (one launch; the split-K pair adds its reduce).
+        # The decode step API: every sequence's new token is written into the cache, then the
+        # decode runs. With its default the write is a launch of its own for these batch sizes
+        # (more than 64 sequence x kv-head rows), else the decode kernel writes the tokens.
         def step():
             ops.decode_step(w.out, w.q, w.new_k, w.new_v, w.k_cache, w.v_cache, w.block_table,
                             w.context_lens, scale, BLOCK, k_scales=w.k_scales,
                             v_scales=w.v_scales, k_scale=w.k_fix, v_scale=w.v_fix,
                             splitk=use_split, validate=validate)
-        return step, dec_launches
+        fused = w.q.shape[0] * w.k_cache.shape[1] <= 64
+        return step, dec_launches + (0 if fused else 1)
     return decode, dec_launches
 
 

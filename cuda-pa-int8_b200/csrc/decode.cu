@@ -714,6 +714,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // With a decode step, wr receives the sequence whose new token lies in the page (the last
   // page of a segment whose context and block id are valid), else -1.
   const bool step_write = a.new_k != nullptr;
+  const uint64_t pol = l2_policy_evict_first();
   // Page jbase + lane of the range: the address of its block id, its (kv_head << 3) | subpage
   // and, for a decode step, the sequence whose new token it holds (else -1).
   auto page_ref = [&](int jbase, int& meta, int& wr) -> const int* {
@@ -789,24 +790,25 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           bulk_g2s(rd + D * 2, static_cast<const uint8_t*>(a.new_v) + so, D * 2, bar);
         }
       }
+      // The cache pages stream through L2 marked evict-first.
       if constexpr (BYTE) {
-        tma_load_3d(kd, &tm_k, bar, sub * 128, 0, row);
+        tma_load_3d_hint(kd, &tm_k, bar, sub * 128, 0, row, pol);
       } else {
-        tma_load_4d(kd, &tm_k, bar, 0, sub * 2, 0, row);
+        tma_load_4d_hint(kd, &tm_k, bar, 0, sub * 2, 0, row, pol);
       }
       if (a.bulk) {
-        bulk_g2s(vd, a.v_base + (size_t)row * C::VT, C::VT, bar);
+        bulk_g2s_hint(vd, a.v_base + (size_t)row * C::VT, C::VT, bar, pol);
         if constexpr (BYTE) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
-          bulk_g2s(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar);
-          bulk_g2s(sd + kVsOff, a.vs_base + (size_t)row * kSubTokens, 64, bar);
+          bulk_g2s_hint(sd, a.ks_base + (size_t)row * kSubTokens, 64, bar, pol);
+          bulk_g2s_hint(sd + kVsOff, a.vs_base + (size_t)row * kSubTokens, 64, bar, pol);
         }
       } else {
-        tma_load_3d(vd, &tm_v, bar, sub * kSubTokens, 0, row);
+        tma_load_3d_hint(vd, &tm_v, bar, sub * kSubTokens, 0, row, pol);
         if constexpr (BYTE) {
           uint8_t* sd = s_tiles + (warp * DEPTH + s) * C::ST;
-          tma_load_2d(sd, &tm_ks, bar, sub * kSubTokens, row);
-          tma_load_2d(sd + kVsOff, &tm_vs, bar, sub * kSubTokens, row);
+          tma_load_2d_hint(sd, &tm_ks, bar, sub * kSubTokens, row, pol);
+          tma_load_2d_hint(sd + kVsOff, &tm_vs, bar, sub * kSubTokens, row, pol);
         }
       }
     }
@@ -905,7 +907,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
     // ---- stage -> registers, then hand the stage back to the TMA right away -------------------
     const int valid = min(kSubTokens, cctx - (csp + k) * kSubTokens);
-    if (step_write) {
+    // Decode step: only a segment's last page can hold a sequence's new token, so no other
+    // page reads the stage's record.
+    if (step_write && csp + k == cpg - 1) {
       const int wrow = s_wrow[warp][s];
       if (wrow >= 0) merge_new_token(s, wrow, valid - 1, (cctx - 1) % a.bs);
     }

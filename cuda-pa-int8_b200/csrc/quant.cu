@@ -76,10 +76,12 @@ __global__ void __launch_bounds__(256) step_rows_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
-// Block-granular prefill: one warp per (sequence, block, kv-head, K|V) page, 16 tokens at a
-// time. A lane holds four consecutive head_dim values of each of the 16 rows (one vector load
-// per row, all in flight together), the warp reduces the 16 row maxima together, and the lane
-// writes the quantised (or fp16) values straight into the page layout with 16-byte stores:
+// Block-granular prefill: one warp per (sequence, block, kv-head): its K page, then its V
+// page, 16 tokens at a time. A lane holds four consecutive head_dim values of each of the 16
+// rows (one vector load per row; with 16-bit inputs the K and V rows are all requested before
+// any is used, so the V loads overlap the K page's work), the warp reduces the 16 row maxima
+// together, and the lane writes the quantised (or fp16) values straight into the page layout
+// with 16-byte stores:
 //   K page [D/8][bs][8]: the lane pair (2c, 2c+1) owns 8-wide chunk c; after the pair swaps
 //     half of its words, lane 2c writes the group's tokens 0-7 and lane 2c+1 tokens 8-15;
 //   V page [D][bs]: lane l owns head_dim rows 4l..4l+3, 16 consecutive tokens each.
@@ -87,23 +89,27 @@ __global__ void __launch_bounds__(256) step_rows_kernel(
 // as zeros with scale 0.
 // ---------------------------------------------------------------------------------------
 constexpr int kPrefillThreads = 256;
-constexpr int kPrefillBlocksPerCta = kPrefillThreads / 64;  // a K warp and a V warp per block
+constexpr int kPrefillBlocksPerCta = kPrefillThreads / 32;  // one block (K and V) per warp
 
-// The four consecutive input values of one lane (8 bytes for 16-bit inputs, 16 for fp32).
-__device__ __forceinline__ void load4(const __half* p, float (&x)[4]) {
-  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+// A lane's four consecutive input values as loaded (8 bytes for 16-bit inputs, 16 for fp32).
+template <typename T> struct Raw4 { using type = uint2; };
+template <> struct Raw4<float> { using type = float4; };
+
+template <typename T>
+__device__ __forceinline__ typename Raw4<T>::type load_raw4(const T* p) {
+  return __ldg(reinterpret_cast<const typename Raw4<T>::type*>(p));
+}
+__device__ __forceinline__ void unpack4(uint2 u, const __half*, float (&x)[4]) {
   const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
   const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
   x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
 }
-__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&x)[4]) {
-  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+__device__ __forceinline__ void unpack4(uint2 u, const __nv_bfloat16*, float (&x)[4]) {
   const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
   const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
   x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
 }
-__device__ __forceinline__ void load4(const float* p, float (&x)[4]) {
-  const float4 u = __ldg(reinterpret_cast<const float4*>(p));
+__device__ __forceinline__ void unpack4(float4 u, const float*, float (&x)[4]) {
   x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
 }
 
@@ -112,19 +118,45 @@ __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// One token's four int8 bytes, quant1(x[e], s) each, as one word (element 0 in the low byte).
+// y = x * inv is rounded to an integer by adding and subtracting 1.5 * 2^23, whose sum's low
+// byte is the int8 byte; that is quant1 unless some y lies within 2^-14 of a half-integer
+// (|y - x/s| < 2^-15 for |y| < 256, see quant_fast) or outside [-127.5, 127.5] (the clamp),
+// or s is 0, where the division decides for the whole token.
+__device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, float inv) {
+  constexpr float kRound = 12582912.f;
+  float dmax = 0.f, ymax = 0.f;
+  uint32_t bits[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float y = __fmul_rn(x[e], inv);
+    const float s1 = __fadd_rn(y, kRound);
+    dmax = fmaxf(dmax, fabsf(__fsub_rn(y, __fsub_rn(s1, kRound))));
+    ymax = fmaxf(ymax, fabsf(y));
+    bits[e] = __float_as_uint(s1);
+  }
+  if (dmax < 0.5f - 0x1p-14f && ymax < 127.5f && s != 0.f)  // s finite and nonzero: y finite
+    return __byte_perm(__byte_perm(bits[0], bits[1], 0x0040), __byte_perm(bits[2], bits[3], 0x0040),
+                       0x5410);
+  return ((uint32_t)(uint8_t)quant1(x[0], s)) | ((uint32_t)(uint8_t)quant1(x[1], s) << 8) |
+         ((uint32_t)(uint8_t)quant1(x[2], s) << 16) | ((uint32_t)(uint8_t)quant1(x[3], s) << 24);
+}
+
 template <typename T, bool I8, int D>
-__global__ void __launch_bounds__(kPrefillThreads, 2) prefill_kernel(
+__global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int L, int KVH,
     const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
     void* __restrict__ k_cache, void* __restrict__ v_cache, float* __restrict__ k_scales,
     float* __restrict__ v_scales, int NB, int bs, const float* __restrict__ kfix,
     const float* __restrict__ vfix, int* status) {
   static_assert(D == 128, "a lane holds four consecutive head_dim values");
+  using R = typename Raw4<T>::type;
+  constexpr bool kBoth = sizeof(T) == 2;  // K and V rows held together (16-bit inputs)
   constexpr unsigned kAll = 0xffffffffu;
   constexpr int ELEM = I8 ? 1 : 2;
+  constexpr int KW = I8 ? 1 : 2;  // words of a lane's four values: int8 one, fp16 two
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x * kPrefillBlocksPerCta + (warp >> 1);
-  const bool is_v = (warp & 1) != 0;
+  const int j = blockIdx.x * kPrefillBlocksPerCta + warp;
   const int kvh = blockIdx.y;
   const int b = blockIdx.z;
   int ctx = __ldg(context_lens + b);
@@ -137,40 +169,33 @@ __global__ void __launch_bounds__(kPrefillThreads, 2) prefill_kernel(
   if (j >= (ctx + bs - 1) / bs) return;  // warp-uniform
   const int blk = __ldg(block_table + (size_t)b * max_blocks + j);
   if (blk < 0 || blk >= NB) {
-    if (lane == 0 && !is_v) flag_error(status, PA_ERR_BLOCK_ID);
+    if (lane == 0) flag_error(status, PA_ERR_BLOCK_ID);
     return;
   }
   const size_t page = (size_t)blk * KVH + kvh;
   const size_t tstride = (size_t)KVH * D;
-  const T* src = (is_v ? v : k) + ((size_t)b * L * KVH + kvh) * D + lane * 4;
-  uint8_t* pg = reinterpret_cast<uint8_t*>(is_v ? v_cache : k_cache) + page * (size_t)D * bs * ELEM;
-  float* scl = (is_v ? v_scales : k_scales) + page * bs;
-  const float* fix = is_v ? vfix : kfix;
-  const int c = lane >> 1;       // K: the lane pair's 8-wide chunk
-  const int hlf = lane & 1;      // K: which half of the chunk the lane holds
+  const size_t row0 = ((size_t)b * L * KVH + kvh) * D + lane * 4;
+  const int c = lane >> 1;   // K: the lane pair's 8-wide chunk
+  const int hlf = lane & 1;  // K: which half of the chunk the lane holds
 
-  for (int g0 = 0; g0 < bs; g0 += 16) {
-    const int valid = min(16, ctx - (j * bs + g0));  // rows of this group inside the context
-    float x[16][4];
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      if (t < valid) {
-        load4(src + (size_t)(j * bs + g0 + t) * tstride, x[t]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) x[t][e] = 0.f;
-      }
-    }
-    constexpr int KW = I8 ? 1 : 2;  // words of a lane's four values: int8 one, fp16 two
+  // Quantise (or round to fp16) and store one page's 16-token group from its raw rows.
+  auto page_group = [&](const R (&raw)[16], bool is_v, int g0, int valid) {
+    uint8_t* pg =
+        reinterpret_cast<uint8_t*>(is_v ? v_cache : k_cache) + page * (size_t)D * bs * ELEM;
     // Per token, the lane's four values as stored: int8 bytes (zero past the context) or fp16.
     uint32_t kw[16][KW];
     if constexpr (I8) {
       // Row maxima, reduced together: after the steps over lane masks 16, 8, 4, 2 lane l holds
-      // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it.
+      // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it. (The
+      // values are unpacked from the raw rows again where they are quantised, so that only the
+      // raw rows stay live.)
       float m[16];
 #pragma unroll
-      for (int t = 0; t < 16; ++t)
-        m[t] = fmaxf(fmaxf(fabsf(x[t][0]), fabsf(x[t][1])), fmaxf(fabsf(x[t][2]), fabsf(x[t][3])));
+      for (int t = 0; t < 16; ++t) {
+        float x[4];
+        unpack4(raw[t], static_cast<const T*>(nullptr), x);
+        m[t] = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+      }
 #pragma unroll
       for (int h = 8, msk = 16; h >= 1; h >>= 1, msk >>= 1) {
         const bool up = (lane & msk) != 0;
@@ -183,26 +208,26 @@ __global__ void __launch_bounds__(kPrefillThreads, 2) prefill_kernel(
       }
       const float am = fmaxf(m[0], __shfl_xor_sync(kAll, m[0], 1));
       const int row = lane >> 1;
+      const float* fix = is_v ? vfix : kfix;
       float s = 0.f;
       if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
       const float inv = __frcp_rn(s);
-      if (hlf == 0) scl[g0 + row] = s;
+      if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const float st = __shfl_sync(kAll, s, 2 * t);
         const float it = __shfl_sync(kAll, inv, 2 * t);
-        uint32_t w = 0u;
-        if (t < valid) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) w |= (uint32_t)(quant_fast(x[t][e], st, it) & 0xff) << (8 * e);
-        }
-        kw[t][0] = w;
+        float x[4];
+        unpack4(raw[t], static_cast<const T*>(nullptr), x);
+        kw[t][0] = t < valid ? quant4(x, st, it) : 0u;
       }
     } else {
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        kw[t][0] = half2_bits(x[t][0], x[t][1]);
-        kw[t][1] = half2_bits(x[t][2], x[t][3]);
+        float x[4];
+        unpack4(raw[t], static_cast<const T*>(nullptr), x);
+        kw[t][0] = half2_bits(x[0], x[1]);
+        kw[t][1] = half2_bits(x[2], x[3]);
       }
     }
     if (!is_v) {
@@ -254,6 +279,33 @@ __global__ void __launch_bounds__(kPrefillThreads, 2) prefill_kernel(
           *reinterpret_cast<uint4*>(dst + 16 * u) =
               make_uint4(vw[4 * u], vw[4 * u + 1], vw[4 * u + 2], vw[4 * u + 3]);
       }
+    }
+  };
+  auto load_rows = [&](const T* src, int t0, int valid, R (&raw)[16]) {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      if (t < valid) {
+        raw[t] = load_raw4(src + row0 + (size_t)(t0 + t) * tstride);
+      } else {
+        raw[t] = R{};
+      }
+    }
+  };
+
+  for (int g0 = 0; g0 < bs; g0 += 16) {
+    const int t0 = j * bs + g0;
+    const int valid = min(16, ctx - t0);  // rows of this group inside the context
+    R rk[16];
+    load_rows(k, t0, valid, rk);
+    if constexpr (kBoth) {
+      R rv[16];
+      load_rows(v, t0, valid, rv);
+      page_group(rk, false, g0, valid);
+      page_group(rv, true, g0, valid);
+    } else {
+      page_group(rk, false, g0, valid);
+      load_rows(v, t0, valid, rk);
+      page_group(rk, true, g0, valid);
     }
   }
 }

@@ -319,7 +319,7 @@ class DecodePlan:
 
 def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_lens, scale,
                 block_size=16, *, k_scales=None, v_scales=None, k_scale=None, v_scale=None,
-                splitk=False, fused=True, validate=True, host_context_lens=None):
+                splitk=False, fused=None, validate=True, host_context_lens=None):
     """One decode step: append every sequence's new token to the cache, then decode.
 
     context_lens already counts the new token: new_k / new_v [num_seqs, kv_heads, head_dim]
@@ -331,7 +331,10 @@ def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_len
     qwen_paged_attn.py:61-73) for a whole batch in one call. With fused=True (and at most 16 q
     heads per kv head) the decode kernel writes each token itself just before reading its
     page, so a step is one launch (two with splitk); fused=False runs the write as its own
-    kernel first. Both give bit-identical caches and outputs.
+    kernel first. Both give bit-identical caches and outputs. The default (fused=None) fuses
+    small batches (at most 64 sequence x kv-head rows), where the saved launch dominates, and
+    writes larger ones first: on a B200 the separate write measured 0.4 % faster at 128 rows
+    and 2 % faster at 1024 rows, because the fused write lengthens the warps that carry it.
 
     With validate=False the call does no host synchronisation and allocates nothing once the
     stream's workspace exists, so after one call on a stream it can be captured in a CUDA
@@ -342,6 +345,8 @@ def decode_step(out, q, new_k, new_v, k_cache, v_cache, block_table, context_len
     B, H, KVH, D, NB = _check_decode_args(out, q, k_cache, v_cache, block_table, context_lens,
                                           block_size, kind, k_scales, v_scales)
     _check_rows(new_k, new_v)
+    if fused is None:
+        fused = B * KVH <= 64
     _require(tuple(new_k.shape) == (B, KVH, D), "new_k/new_v must be [num_seqs, kv_heads, "
              "head_dim]")
     _require(new_k.device == q.device, "new_k/new_v must be on q's device")

@@ -96,8 +96,9 @@ class PagedKVCache:
     def append_and_decode(self, layer_idx, k, v, q, scale, out=None):
         """decode_append(layer_idx, k, v) followed by the split-K decode of q [1, num_q_heads,
         head_dim] over the layer's cache -- the bridge's decode step
-        (benchmarks/int8_bridge/qwen_paged_attn.py:61-73) -- as one fused call (the token is
-        written by the decode kernel). Returns out [1, num_q_heads, head_dim] fp16."""
+        (benchmarks/int8_bridge/qwen_paged_attn.py:61-73) -- as one call (for this one
+        sequence the token is written by the decode kernel itself). Returns out
+        [1, num_q_heads, head_dim] fp16."""
         t = self.lengths[layer_idx]
         H, D = self.num_kv_heads, self.head_dim
         q = q.contiguous()
