@@ -9,6 +9,8 @@
 #include "pa_internal.h"
 #include "pa_rows.cuh"
 
+#include <algorithm>
+
 namespace pa {
 namespace {
 
@@ -76,20 +78,22 @@ __global__ void __launch_bounds__(256) step_rows_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
-// Block-granular prefill: one warp per (sequence, block, kv-head): its K page, then its V
-// page, 16 tokens at a time. A lane holds four consecutive head_dim values of each of the 16
-// rows (one vector load per row; with 16-bit inputs the K and V rows are all requested before
-// any is used, so the V loads overlap the K page's work), the warp reduces the 16 row maxima
-// together, and the lane writes the quantised (or fp16) values straight into the page layout
-// with 16-byte stores:
+// Block-granular prefill. The work is cut into 16-token groups of one (sequence, block,
+// kv-head); every group of a block inside the context is written, and tokens past the
+// context in a sequence's last block are written as zeros with scale 0. CTAs are persistent
+// (as many as fit on the GPU) and each warp walks its share of the groups with a two-deep
+// pipeline: while it works on one group, the next group's K and V rows are copied into its
+// shared-memory buffer by cp.async (each lane copies, and later reads, only its own four
+// head_dim values of each row). For a group a lane holds four consecutive head_dim values of
+// each of the 16 rows, the warp reduces the 16 row maxima together, and the lane writes the
+// quantised (or fp16) values straight into the page layout with 16-byte stores:
 //   K page [D/8][bs][8]: the lane pair (2c, 2c+1) owns 8-wide chunk c; after the pair swaps
 //     half of its words, lane 2c writes the group's tokens 0-7 and lane 2c+1 tokens 8-15;
 //   V page [D][bs]: lane l owns head_dim rows 4l..4l+3, 16 consecutive tokens each.
-// No shared memory and no per-element index arithmetic. Tokens past the context are written
-// as zeros with scale 0.
 // ---------------------------------------------------------------------------------------
-constexpr int kPrefillThreads = 256;
-constexpr int kPrefillBlocksPerCta = kPrefillThreads / 32;  // one block (K and V) per warp
+constexpr int kPrefillThreads = 128;
+constexpr int kPrefillWarps = kPrefillThreads / 32;
+constexpr int kLensSmem = 1024;  // sequence lengths staged in shared memory
 
 // A lane's four consecutive input values as loaded (8 bytes for 16-bit inputs, 16 for fp32).
 template <typename T> struct Raw4 { using type = uint2; };
@@ -118,77 +122,179 @@ __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Packed fp32 pairs (sm_100's two-wide fp32 instructions; each half rounds as the scalar op).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // One token's four int8 bytes, quant1(x[e], s) each, as one word (element 0 in the low byte).
 // y = x * inv is rounded to an integer by adding and subtracting 1.5 * 2^23, whose sum's low
 // byte is the int8 byte; that is quant1 unless some y lies within 2^-14 of a half-integer
-// (|y - x/s| < 2^-15 for |y| < 256, see quant_fast) or outside [-127.5, 127.5] (the clamp),
-// or s is 0, where the division decides for the whole token.
-__device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, float inv) {
-  constexpr float kRound = 12582912.f;
+// (|y - x/s| < 2^-15 for |y| < 256, see quant_fast), or s is 0, where the division decides for
+// the whole token. With `ranged` the token also takes the division when some |y| >= 127.5 (the
+// clamp); rows need that only with a fixed scale or a scale below 2^-14, since otherwise
+// s = T(amax / 127) keeps every |x / s| below 127.5. The arithmetic runs on value pairs.
+template <bool kRanged>
+__device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, uint64_t inv2,
+                                           bool ranged) {
+  const uint64_t kr = f2_pack(12582912.f, 12582912.f);
   float dmax = 0.f, ymax = 0.f;
   uint32_t bits[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float y = __fmul_rn(x[e], inv);
-    const float s1 = __fadd_rn(y, kRound);
-    dmax = fmaxf(dmax, fabsf(__fsub_rn(y, __fsub_rn(s1, kRound))));
-    ymax = fmaxf(ymax, fabsf(y));
-    bits[e] = __float_as_uint(s1);
+  for (int h = 0; h < 2; ++h) {
+    const uint64_t y = f2_mul(f2_pack(x[2 * h], x[2 * h + 1]), inv2);
+    const uint64_t s1 = f2_add(y, kr);
+    const uint64_t d = f2_sub(y, f2_sub(s1, kr));
+    float d0, d1, y0, y1, b0, b1;
+    f2_unpack(d, d0, d1);
+    f2_unpack(s1, b0, b1);
+    dmax = fmaxf(dmax, fmaxf(fabsf(d0), fabsf(d1)));
+    if (kRanged || ranged) {
+      f2_unpack(y, y0, y1);
+      ymax = fmaxf(ymax, fmaxf(fabsf(y0), fabsf(y1)));
+    }
+    bits[2 * h] = __float_as_uint(b0);
+    bits[2 * h + 1] = __float_as_uint(b1);
   }
-  if (dmax < 0.5f - 0x1p-14f && ymax < 127.5f && s != 0.f)  // s finite and nonzero: y finite
+  // NaN d (s = 0) fails the first test; ymax stays 0 unless checked.
+  if (dmax < 0.5f - 0x1p-14f && ymax < 127.5f && s != 0.f)
     return __byte_perm(__byte_perm(bits[0], bits[1], 0x0040), __byte_perm(bits[2], bits[3], 0x0040),
                        0x5410);
   return ((uint32_t)(uint8_t)quant1(x[0], s)) | ((uint32_t)(uint8_t)quant1(x[1], s) << 8) |
          ((uint32_t)(uint8_t)quant1(x[2], s) << 16) | ((uint32_t)(uint8_t)quant1(x[3], s) << 24);
 }
 
+// cp.async of one lane's four input values (8 or 16 bytes).
+template <typename T>
+__device__ __forceinline__ void cp_async_raw4(void* smem_dst, const T* gsrc) {
+  if constexpr (sizeof(T) == 2) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+  } else {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+  }
+}
+
+// Shared memory of one warp's pipeline stage: 16 K rows then 16 V rows of D values.
+template <typename T, int D>
+__host__ __device__ constexpr int prefill_stage_bytes() {
+  return 2 * 16 * D * (int)sizeof(T);
+}
+
 template <typename T, bool I8, int D>
-__global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(
-    const T* __restrict__ k, const T* __restrict__ v, int L, int KVH,
+__global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, int S, int L, int KVH,
     const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
     void* __restrict__ k_cache, void* __restrict__ v_cache, float* __restrict__ k_scales,
     float* __restrict__ v_scales, int NB, int bs, const float* __restrict__ kfix,
     const float* __restrict__ vfix, int* status) {
   static_assert(D == 128, "a lane holds four consecutive head_dim values");
   using R = typename Raw4<T>::type;
-  constexpr bool kBoth = sizeof(T) == 2;  // K and V rows held together (16-bit inputs)
   constexpr unsigned kAll = 0xffffffffu;
   constexpr int ELEM = I8 ? 1 : 2;
   constexpr int KW = I8 ? 1 : 2;  // words of a lane's four values: int8 one, fp16 two
+  constexpr int SB = prefill_stage_bytes<T, D>();
+  constexpr int ROWB = D * (int)sizeof(T);
+  extern __shared__ __align__(16) uint8_t psm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x * kPrefillBlocksPerCta + warp;
-  const int kvh = blockIdx.y;
-  const int b = blockIdx.z;
-  int ctx = __ldg(context_lens + b);
-  const int cap = min(L, max_blocks * bs);
-  if (ctx > cap) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && kvh == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
-    ctx = cap;
-  }
-  if (ctx < 0) ctx = 0;
-  if (j >= (ctx + bs - 1) / bs) return;  // warp-uniform
-  const int blk = __ldg(block_table + (size_t)b * max_blocks + j);
-  if (blk < 0 || blk >= NB) {
-    if (lane == 0) flag_error(status, PA_ERR_BLOCK_ID);
-    return;
-  }
-  const size_t page = (size_t)blk * KVH + kvh;
-  const size_t tstride = (size_t)KVH * D;
-  const size_t row0 = ((size_t)b * L * KVH + kvh) * D + lane * 4;
+  uint8_t* stage0 = psm + (size_t)warp * 2 * SB;
   const int c = lane >> 1;   // K: the lane pair's 8-wide chunk
   const int hlf = lane & 1;  // K: which half of the chunk the lane holds
+  const int gpb = bs / 16;   // groups per block
+  const int cap = min(L, max_blocks * bs);
+  const size_t tstride = (size_t)KVH * D;
+  const long long total = (long long)S * KVH * max_blocks * gpb;
+  const long long W = (long long)gridDim.x * kPrefillWarps;
+
+  // Group g of the flattened (sequence, kv-head, block, group) space, when it is to be
+  // written (its block lies inside the context): sequence, kv head, first token, rows inside
+  // the context (<= 0 for a group past the context in the last block), page row.
+  // The sequences' lengths, clamped to the buffers, in shared memory (the first kLensSmem;
+  // later ones are read from global memory).
+  int* s_ctx = reinterpret_cast<int*>(psm + (size_t)kPrefillWarps * 2 * SB);
+  for (int i = threadIdx.x; i < min(S, kLensSmem); i += kPrefillThreads) {
+    int ctx = __ldg(context_lens + i);
+    if (ctx > cap) {
+      if (blockIdx.x == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
+      ctx = cap;
+    }
+    s_ctx[i] = ctx < 0 ? 0 : ctx;
+  }
+  __syncthreads();
+  auto ctx_of = [&](int b) -> int {
+    if (b < kLensSmem) return s_ctx[b];
+    const int ctx = __ldg(context_lens + b);
+    return ctx > cap ? cap : (ctx < 0 ? 0 : ctx);
+  };
+  // A group to write: sequence, kv head, first token, rows inside the context (<= 0 for a
+  // group past the context in the last block) and its block id, loaded here and first used
+  // when the group is processed, one pipeline step later.
+  struct Grp {
+    int b, kvh, t0, valid, blk;
+  };
+  auto decode_grp = [&](long long g, Grp& r) -> bool {
+    const int jg = (int)(g % ((long long)max_blocks * gpb));
+    const long long bk = g / ((long long)max_blocks * gpb);
+    r.kvh = (int)(bk % KVH);
+    r.b = (int)(bk / KVH);
+    const int j = jg / gpb;
+    r.t0 = j * bs + (jg - j * gpb) * 16;
+    const int ctx = ctx_of(r.b);
+    if (j >= (ctx + bs - 1) / bs) return false;  // past the sequence's last block
+    r.valid = min(16, ctx - r.t0);
+    r.blk = __ldg(block_table + (size_t)r.b * max_blocks + j);
+    return true;
+  };
+  // Copy the group's rows inside the context into stage st (one commit group).
+  auto issue = [&](const Grp& gr, int st) {
+    uint8_t* sb = stage0 + st * SB + lane * 4 * (int)sizeof(T);
+    const size_t base = ((size_t)gr.b * L * KVH + gr.kvh) * D + lane * 4;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      if (t < gr.valid) {
+        const size_t off = base + (size_t)(gr.t0 + t) * tstride;
+        cp_async_raw4(sb + t * ROWB, k + off);
+        cp_async_raw4(sb + (16 + t) * ROWB, v + off);
+      }
+    }
+    cp_async_commit();
+  };
 
   // Quantise (or round to fp16) and store one page's 16-token group from its raw rows.
-  auto page_group = [&](const R (&raw)[16], bool is_v, int g0, int valid) {
+  auto page_group = [&](const R (&raw)[16], bool is_v, const Grp& gr) {
+    const int g0 = gr.t0 % bs;
+    const int valid = gr.valid;
+    const size_t page = (size_t)gr.blk * KVH + gr.kvh;
     uint8_t* pg =
         reinterpret_cast<uint8_t*>(is_v ? v_cache : k_cache) + page * (size_t)D * bs * ELEM;
     // Per token, the lane's four values as stored: int8 bytes (zero past the context) or fp16.
     uint32_t kw[16][KW];
     if constexpr (I8) {
       // Row maxima, reduced together: after the steps over lane masks 16, 8, 4, 2 lane l holds
-      // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it. (The
-      // values are unpacked from the raw rows again where they are quantised, so that only the
-      // raw rows stay live.)
+      // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it.
       float m[16];
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
@@ -213,13 +319,15 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(
       if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
       const float inv = __frcp_rn(s);
       if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
+      // The clamp can bind only with a fixed scale or a scale below 2^-14 (fp16 subnormal).
+      const bool ranged = __any_sync(kAll, fix != nullptr || (s > 0.f && s < 0x1p-14f));
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const float st = __shfl_sync(kAll, s, 2 * t);
         const float it = __shfl_sync(kAll, inv, 2 * t);
         float x[4];
         unpack4(raw[t], static_cast<const T*>(nullptr), x);
-        kw[t][0] = t < valid ? quant4(x, st, it) : 0u;
+        kw[t][0] = t < valid ? quant4<false>(x, st, f2_pack(it, it), ranged) : 0u;
       }
     } else {
 #pragma unroll
@@ -281,32 +389,50 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(
       }
     }
   };
-  auto load_rows = [&](const T* src, int t0, int valid, R (&raw)[16]) {
+  // The group's K (which = 0) or V rows of stage st, zeros past the context.
+  auto read_rows = [&](int st, int which, int valid, R (&raw)[16]) {
+    const uint8_t* sb = stage0 + st * SB + which * 16 * ROWB + lane * 4 * (int)sizeof(T);
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      if (t < valid) {
-        raw[t] = load_raw4(src + row0 + (size_t)(t0 + t) * tstride);
-      } else {
-        raw[t] = R{};
-      }
-    }
+    for (int t = 0; t < 16; ++t)
+      raw[t] = t < valid ? *reinterpret_cast<const R*>(sb + t * ROWB) : R{};
   };
 
-  for (int g0 = 0; g0 < bs; g0 += 16) {
-    const int t0 = j * bs + g0;
-    const int valid = min(16, ctx - t0);  // rows of this group inside the context
-    R rk[16];
-    load_rows(k, t0, valid, rk);
-    if constexpr (kBoth) {
-      R rv[16];
-      load_rows(v, t0, valid, rv);
-      page_group(rk, false, g0, valid);
-      page_group(rv, true, g0, valid);
-    } else {
-      page_group(rk, false, g0, valid);
-      load_rows(v, t0, valid, rk);
-      page_group(rk, true, g0, valid);
+  // The groups to write, in this warp's share of the flattened space.
+  long long g = (long long)blockIdx.x * kPrefillWarps + warp;
+  auto next_grp = [&](Grp& out) -> bool {
+    while (g < total) {
+      const bool ok = decode_grp(g, out);
+      g += W;
+      if (ok) return true;
     }
+    return false;
+  };
+  Grp cur, nxt;
+  bool have = next_grp(cur);
+  if (have) issue(cur, 0);
+  int st = 0;
+  while (have) {
+    const bool more = next_grp(nxt);
+    if (more) {
+      issue(nxt, st ^ 1);
+      cp_async_wait_group_1();
+    } else {
+      cp_async_wait_all();
+    }
+    __syncwarp();
+    if (cur.blk >= 0 && cur.blk < NB) {
+      R raw[16];
+      read_rows(st, 0, cur.valid, raw);
+      page_group(raw, false, cur);
+      read_rows(st, 1, cur.valid, raw);
+      page_group(raw, true, cur);
+    } else if (lane == 0) {
+      flag_error(status, PA_ERR_BLOCK_ID);
+    }
+    __syncwarp();  // the stage's rows are read before the next issue overwrites it
+    cur = nxt;
+    have = more;
+    st ^= 1;
   }
 }
 
@@ -392,12 +518,24 @@ cudaError_t launch_prefill_t(bool i8, const void* k, const void* v, int S, int L
                              float* ks, float* vs, int NB, int bs, const float* kf,
                              const float* vf, int* status, cudaStream_t st) {
   if (S == 0 || max_blocks == 0) return cudaSuccess;
-  const dim3 grid((max_blocks + kPrefillBlocksPerCta - 1) / kPrefillBlocksPerCta, KVH, S);
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
   auto kern = i8 ? prefill_kernel<T, true, 128> : prefill_kernel<T, false, 128>;
-  kern<<<grid, kPrefillThreads, 0, st>>>(kk, vv, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs, NB,
-                                         bs, kf, vf, status);
+  // Persistent CTAs: as many as fit on the GPU, never more than there are groups.
+  const int smem = kPrefillWarps * 2 * prefill_stage_bytes<T, 128>() + kLensSmem * 4;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0, per_sm = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPrefillThreads, smem);
+  if (e != cudaSuccess) return e;
+  const long long groups = (long long)S * KVH * max_blocks * (bs / 16);
+  const long long want = (groups + kPrefillWarps - 1) / kPrefillWarps;
+  const int grid = (int)std::min<long long>(want, (long long)sms * std::max(per_sm, 1));
+  kern<<<grid, kPrefillThreads, smem, st>>>(kk, vv, S, L, KVH, bt, cl, max_blocks, kc, vc, ks,
+                                            vs, NB, bs, kf, vf, status);
   return cudaGetLastError();
 }
 

@@ -302,3 +302,27 @@ def test_quantizer_near_half_integers_bit_exact(scale):
     assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
     sc = np.full((2, L, KVH), s, np.float32)
     assert _bits_equal(ks, pa_oracle.scatter_scales(sc, cl, bt, 8, KVH, 16))
+
+
+def test_prefill_many_short_sequences_bit_exact():
+    """More sequences than the prefill kernel stages lengths for in shared memory (1024),
+    lengths 0-40 (empty sequences write nothing), block size 32: bit-exact with the oracle."""
+    S, KVH, bs = 1100, 1, 32
+    rng = np.random.default_rng(41)
+    cl = rng.integers(0, 41, size=S).astype(np.int32)
+    mb = 2
+    L = int(cl.max())
+    nb = S * mb
+    bt = rng.permutation(nb).astype(np.int32).reshape(S, mb)
+    k = rng.standard_normal((S, L, KVH, 128)).astype(np.float16)
+    v = rng.standard_normal((S, L, KVH, 128)).astype(np.float16)
+    kc, vc, ks, vs = _caches(nb, KVH, bs)
+    tk, tv, tbt, tcl = to_cuda(k, v, bt, cl)
+    _ops().prefill_into_cache(tk, tv, kc, vc, tbt, tcl, bs, k_scales=ks, v_scales=vs)
+    kq, ksc = pa_oracle.quantize_per_token(k, "f16")
+    vq, vsc = pa_oracle.quantize_per_token(v, "f16")
+    okc, ovc = pa_oracle.scatter_paged_cache(kq, vq, cl, bt, nb, bs)
+    assert np.array_equal(kc.cpu().numpy().view(np.uint8), okc.view(np.uint8))
+    assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
+    assert _bits_equal(ks, pa_oracle.scatter_scales(ksc, cl, bt, nb, KVH, bs))
+    assert _bits_equal(vs, pa_oracle.scatter_scales(vsc, cl, bt, nb, KVH, bs))
