@@ -150,10 +150,11 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
 // One token's four int8 bytes, quant1(x[e], s) each, as one word (element 0 in the low byte).
 // y = x * inv is rounded to an integer by adding and subtracting 1.5 * 2^23, whose sum's low
 // byte is the int8 byte; that is quant1 unless some y lies within 2^-14 of a half-integer
-// (|y - x/s| < 2^-15 for |y| < 256, see quant_fast), or s is 0, where the division decides for
-// the whole token. With `ranged` the token also takes the division when some |y| >= 127.5 (the
-// clamp); rows need that only with a fixed scale or a scale below 2^-14, since otherwise
-// s = T(amax / 127) keeps every |x / s| below 127.5. The arithmetic runs on value pairs.
+// (|y - x/s| < 2^-15 for |y| < 256, see quant_fast), or s is 0 or infinite, where the division
+// decides for the whole token. With `ranged` the token also takes the division when some
+// |y| >= 127.5 (the clamp); rows need that only with a fixed scale or a scale below 2^-14,
+// since otherwise s = T(amax / 127) keeps every |x / s| below 127.5. The arithmetic runs on
+// value pairs.
 template <bool kRanged>
 __device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, uint64_t inv2,
                                            bool ranged) {
@@ -176,8 +177,10 @@ __device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, uint64_
     bits[2 * h] = __float_as_uint(b0);
     bits[2 * h + 1] = __float_as_uint(b1);
   }
-  // NaN d (s = 0) fails the first test; ymax stays 0 unless checked.
-  if (dmax < 0.5f - 0x1p-14f && ymax < 127.5f && s != 0.f)
+  // fmaxf drops NaN, so the scales that can produce NaN quotients (0: 0/0, and infinite: an
+  // infinite element over an infinite scale) take the division explicitly; ymax stays 0 unless
+  // checked.
+  if (dmax < 0.5f - 0x1p-14f && ymax < 127.5f && s != 0.f && s < __int_as_float(0x7f800000))
     return __byte_perm(__byte_perm(bits[0], bits[1], 0x0040), __byte_perm(bits[2], bits[3], 0x0040),
                        0x5410);
   return ((uint32_t)(uint8_t)quant1(x[0], s)) | ((uint32_t)(uint8_t)quant1(x[1], s) << 8) |

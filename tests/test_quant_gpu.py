@@ -326,3 +326,44 @@ def test_prefill_many_short_sequences_bit_exact():
     assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
     assert _bits_equal(ks, pa_oracle.scatter_scales(ksc, cl, bt, nb, KVH, bs))
     assert _bits_equal(vs, pa_oracle.scatter_scales(vsc, cl, bt, nb, KVH, bs))
+
+
+@pytest.mark.parametrize("source", ["golden16", "golden32", "goldenbf16"])
+@pytest.mark.parametrize("int8", [True, False])
+def test_prefill_input_dtypes_bit_exact(source, int8):
+    """The prefill scatter with fp16, fp32 and bf16 input rows (the golden rows of the
+    reference quantiser), block size 32, into INT8 and FP16 caches: bit-exact with the oracle
+    (the FP16 cache gets the rows rounded to fp16)."""
+    gold = np.load(os.path.join(GOLD, "quant_rows.npz"))
+    if source == "golden16":
+        x, dtype, tdt = gold["x16"].astype(np.float32), "f16", torch.float16
+    elif source == "golden32":
+        x, dtype, tdt = gold["x32"], "f32", torch.float32
+    else:
+        x = (gold["xbf16_bits"].astype(np.uint32) << 16).view(np.float32)
+        dtype, tdt = "bf16", torch.bfloat16
+    S, KVH, bs = 2, 2, 32
+    L = x.shape[0] // (S * KVH)
+    k = np.ascontiguousarray(x[:S * L * KVH].reshape(S, L, KVH, 128))
+    v = np.ascontiguousarray(k[:, ::-1])
+    cl = np.array([L, L - 5], np.int32)
+    mb = (L + bs - 1) // bs
+    nb = S * mb + 2
+    bt = np.random.default_rng(7).permutation(nb)[:S * mb].astype(np.int32).reshape(S, mb)
+    kc, vc, ks, vs = _caches(nb, KVH, bs, int8)
+    tk = torch.from_numpy(k).to(tdt).cuda()
+    tv = torch.from_numpy(v).to(tdt).cuda()
+    tbt, tcl = to_cuda(bt, cl)
+    kw = dict(k_scales=ks, v_scales=vs) if int8 else {}
+    _ops().prefill_into_cache(tk, tv, kc, vc, tbt, tcl, bs, **kw)
+    if int8:
+        kq, ksc = pa_oracle.quantize_per_token(k, dtype)
+        vq, vsc = pa_oracle.quantize_per_token(v, dtype)
+        okc, ovc = pa_oracle.scatter_paged_cache(kq, vq, cl, bt, nb, bs)
+        assert _bits_equal(ks, pa_oracle.scatter_scales(ksc, cl, bt, nb, KVH, bs))
+        assert _bits_equal(vs, pa_oracle.scatter_scales(vsc, cl, bt, nb, KVH, bs))
+    else:
+        okc, ovc = pa_oracle.scatter_paged_cache(k.astype(np.float16), v.astype(np.float16), cl,
+                                                 bt, nb, bs)
+    assert np.array_equal(kc.cpu().numpy().view(np.uint8), okc.view(np.uint8))
+    assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
