@@ -1429,36 +1429,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// LSE reduce of the split-K pair (and of partials gathered across GPUs). A segment's output is
-// cut into NSL slices of head_dim rows, one CTA per (segment, slice), so that even a few
-// segments spread over the GPU: every CTA of a segment forms the same maxima, weights and
-// denominators from the pieces' m and l, then sums its slice of sum_k w_k O_k. Each output
-// float4 is summed by piece groups (pieces k = g, g + groups, ...) with kRedU loads in flight
-// per thread, and the groups' sums are added in group order, so results are the same from run
-// to run.
+// LSE reduce of the split-K pair (and of partials gathered across GPUs): one CTA of
+// kReduceThreads threads per (sequence, kv-head, head tile) segment, merged cooperatively.
 // ---------------------------------------------------------------------------------------
-constexpr int kReduceThreads = 256;
-constexpr int kRedU = 8;
+constexpr int kReduceThreads = 512;
 
 template <int D, int GT>
-__host__ __device__ constexpr size_t reduce_smem_floats(int np) {
-  // weights [np][GT], per-warp partial maxima / denominators, M and L, then the piece groups'
-  // float4 sums.
-  return ((size_t)np * GT + 3) / 4 * 4 + (kReduceThreads / 32) * GT + 2 * GT +
-         (size_t)kReduceThreads * 4;
-}
-
-template <int D, int GT, int NSL>
-__global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const ReduceArgs a) {
-  constexpr int OUT4 = D / NSL * GT / 4;  // float4 outputs of one slice
-  static_assert(kReduceThreads % OUT4 == 0, "a slice's outputs tile the block");
-  constexpr int PG = kReduceThreads / OUT4;  // piece groups
-  constexpr int NW = kReduceThreads / 32;
+__global__ void __launch_bounds__(kReduceThreads, 1) reduce_kernel(const ReduceArgs a) {
   extern __shared__ __align__(16) float rsm[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int SEGS = a.KVH * a.HT;
   const int segid = blockIdx.x;
-  const int slice = blockIdx.y;
   const int b = segid / SEGS;
   const int seg = segid - b * SEGS;
   const int kvh = seg / a.HT;
@@ -1474,121 +1454,15 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const ReduceArgs
     np = (pages + kSplitPages - 1) / kSplitPages;
   }
   __half* orow = a.out + ((size_t)b * a.H + hbase) * D;
-  constexpr int DS = D / NSL;  // head_dim rows of a slice
-  const int d0 = slice * DS;
   if (np == 0) {
-    for (int i = tid; i < hcnt * DS; i += kReduceThreads)
-      orow[(size_t)(i / DS) * D + d0 + i % DS] = __float2half_rn(0.f);
-    if (tid == 0 && seg == 0 && slice == 0) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
+    for (int i = threadIdx.x; i < hcnt * D; i += blockDim.x) orow[i] = __float2half_rn(0.f);
+    if (threadIdx.x == 0 && seg == 0) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
     return;
   }
   const float* base = a.part + (size_t)segid * a.seg_stride;
-  float* sW = rsm;                                          // [np][GT]
-  float* sRed = sW + ((size_t)np * GT + 3) / 4 * 4;         // [NW][GT]
-  float* sM = sRed + NW * GT;                               // [GT]
-  float* sL = sM + GT;                                      // [GT]
-  float4* sAcc = reinterpret_cast<float4*>(sL + GT);        // [PG][OUT4]
-
-  // Maxima over the pieces.
-  float mx[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) mx[h] = neg_inf();
-  for (int k = tid; k < np; k += kReduceThreads) {
-    const float* mk = base + (size_t)k * a.piece_stride + D * GT;
-#pragma unroll
-    for (int h = 0; h < GT; ++h) mx[h] = fmaxf(mx[h], __ldcg(mk + h));
-  }
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    const float v = warp_max(mx[h]);
-    if (lane == 0) sRed[warp * GT + h] = v;
-  }
-  __syncthreads();
-  if (tid < GT) {
-    float v = neg_inf();
-    for (int w = 0; w < NW; ++w) v = fmaxf(v, sRed[w * GT + tid]);
-    sM[tid] = v;
-  }
-  __syncthreads();
-  // Weights w_k = 2^(m_k - M) and the denominator L = sum_k w_k l_k (each thread sums its
-  // pieces in order, then the warps and the threads in a fixed tree).
-  float ls[GT];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) ls[h] = 0.f;
-  for (int k = tid; k < np; k += kReduceThreads) {
-    const float* mk = base + (size_t)k * a.piece_stride + D * GT;
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      const float M = sM[h];
-      const float w = (M == neg_inf()) ? 0.f : ex2(__ldcg(mk + h) - M);
-      sW[(size_t)k * GT + h] = w;
-      ls[h] += w * __ldcg(mk + GT + h);
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    float v = ls[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) sRed[warp * GT + h] = v;
-  }
-  __syncthreads();
-  if (tid < GT) {
-    float v = 0.f;
-    for (int w = 0; w < NW; ++w) v += sRed[w * GT + tid];
-    sL[tid] = v;
-  }
-  __syncthreads();
-
-  // This thread's float4 of the slice (row d0 + o / (GT/4), heads h0..h0+3) and piece group g.
-  const int o = tid % OUT4;
-  const int g = tid / OUT4;
-  const int h0 = (o % (GT / 4)) * 4;
-  const size_t off4 = (size_t)d0 * GT / 4 + o;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k0 = g; k0 < np; k0 += PG * kRedU) {
-    float4 v[kRedU];
-#pragma unroll
-    for (int u = 0; u < kRedU; ++u) {
-      const int k = k0 + u * PG;
-      v[u] = k < np ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)k * a.piece_stride) +
-                             off4)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < kRedU; ++u) {
-      const int k = k0 + u * PG;
-      if (k < np) {
-        const float* w = sW + (size_t)k * GT + h0;
-        acc.x = fmaf(w[0], v[u].x, acc.x);
-        acc.y = fmaf(w[1], v[u].y, acc.y);
-        acc.z = fmaf(w[2], v[u].z, acc.z);
-        acc.w = fmaf(w[3], v[u].w, acc.w);
-      }
-    }
-  }
-  sAcc[g * OUT4 + o] = acc;
-  __syncthreads();
-  if (g == 0) {
-    for (int g2 = 1; g2 < PG; ++g2) {
-      const float4 t = sAcc[g2 * OUT4 + o];
-      acc.x += t.x;
-      acc.y += t.y;
-      acc.z += t.z;
-      acc.w += t.w;
-    }
-    const int d = d0 + o / (GT / 4);
-    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int h = h0 + e;
-      if (h < hcnt) {
-        const float L = sL[h];
-        orow[(size_t)h * D + d] = __float2half_rn(L > 0.f ? a4[e] / L : 0.f);
-      }
-    }
-  }
-  if (tid < hcnt && slice == 0 && !(sL[tid] > 0.f)) flag_error(a.status, PA_ERR_EMPTY_CONTEXT);
+  coop_combine<D, GT, kReduceThreads, 16>(
+      [&](int k) { return base + (size_t)k * a.piece_stride; }, np, hcnt, orow, nullptr,
+      a.status, rsm);
 }
 
 // Launch shapes per (cache dtype, head tile): warps per CTA (one CTA per SM) and ring depth
@@ -1680,43 +1554,27 @@ cudaError_t launch_selftest_wait(int* status, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-namespace {
-template <int GT, int NSL>
-cudaError_t launch_reduce_t(const ReduceArgs& a, int segs, int max_pieces, cudaStream_t stream) {
-  const size_t smem = reduce_smem_floats<128, GT>(max_pieces) * sizeof(float);
-  auto kern = reduce_kernel<128, GT, NSL>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  kern<<<dim3(segs, NSL), kReduceThreads, smem, stream>>>(a);
-  return cudaGetLastError();
-}
-}  // namespace
-
 cudaError_t launch_reduce(int gt, const ReduceArgs& a, int max_pieces, cudaStream_t stream) {
   const int segs = a.B * a.KVH * a.HT;
   if (segs == 0) return cudaSuccess;
-  if (reduce_smem_floats<128, 16>(max_pieces) * sizeof(float) > 200 * 1024)
-    return cudaErrorInvalidValue;  // more splits than one CTA can weigh (contexts > ~3M tokens)
-  // Slices per segment: enough CTAs to cover the GPU twice over.
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    (void)cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int nsl = segs >= 2 * sms ? 1 : (segs * 2 >= 2 * sms ? 2 : (segs * 4 >= 2 * sms ? 4 : 8));
+  size_t smem;
+  cudaError_t e;
+  if (Coop<128, 16, kReduceThreads, 16>::floats(max_pieces) * sizeof(float) > 200 * 1024)
+    return cudaErrorInvalidValue;  // more splits than one CTA can merge (contexts > ~3M tokens)
   if (gt == 8) {
-    switch (nsl) {
-      case 1: return launch_reduce_t<8, 1>(a, segs, max_pieces, stream);
-      case 2: return launch_reduce_t<8, 2>(a, segs, max_pieces, stream);
-      case 4: return launch_reduce_t<8, 4>(a, segs, max_pieces, stream);
-      default: return launch_reduce_t<8, 8>(a, segs, max_pieces, stream);
-    }
+    smem = Coop<128, 8, kReduceThreads, 16>::floats(max_pieces) * sizeof(float);
+    e = cudaFuncSetAttribute(reduce_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    reduce_kernel<128, 8><<<segs, kReduceThreads, smem, stream>>>(a);
+  } else {
+    smem = Coop<128, 16, kReduceThreads, 16>::floats(max_pieces) * sizeof(float);
+    e = cudaFuncSetAttribute(reduce_kernel<128, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    reduce_kernel<128, 16><<<segs, kReduceThreads, smem, stream>>>(a);
   }
-  switch (nsl) {  // 16-row head tiles: at least two slices, so a slice fits the block
-    case 1:
-    case 2: return launch_reduce_t<16, 2>(a, segs, max_pieces, stream);
-    case 4: return launch_reduce_t<16, 4>(a, segs, max_pieces, stream);
-    default: return launch_reduce_t<16, 8>(a, segs, max_pieces, stream);
-  }
+  return cudaGetLastError();
 }
 
 }  // namespace pa
