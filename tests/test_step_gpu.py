@@ -311,3 +311,47 @@ def test_decode_plan_matches_decode_and_rejects_other_shapes():
         with pytest.raises(RuntimeError, match="context_lens must be >= 1"):
             plan.run(host_context_lens=torch.zeros_like(c["cl"].cpu()))
 
+
+
+def test_decode_plans_on_two_streams_overlap_safely():
+    """Two DecodePlans driven from two streams, as a double-buffered serving loop does: each
+    stream gets its own workspace, so decodes in flight on both streams at once give the same
+    bits as the same decodes run one after another on one stream. Each round also uploads the
+    inputs from pinned memory and reads the output back on its stream."""
+    from pa_b200 import ops
+    for kind in ("f16", "i8"):
+        c = _setup(kind, LENS, 12, 2, seed=23)
+        qs = [torch.randn_like(c["q"]) for _ in range(4)]
+        refs = []
+        for q in qs:
+            r = torch.empty_like(q)
+            ops.decode(r, q, c["kc"], c["vc"], c["bt"], c["cl"], SCALE, 16,
+                       k_scales=c["ks"], v_scales=c["vs"])
+            refs.append(r.cpu())
+        streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+        dq = [torch.empty_like(c["q"]) for _ in range(2)]
+        dout = [torch.empty_like(c["q"]) for _ in range(2)]
+        hq = [torch.empty(c["q"].shape, dtype=c["q"].dtype, pin_memory=True) for _ in range(4)]
+        hout = [torch.empty(c["q"].shape, dtype=c["q"].dtype, pin_memory=True)
+                for _ in range(4)]
+        for h, q in zip(hq, qs):
+            h.copy_(q.cpu())
+        plans = [ops.DecodePlan(dout[i], dq[i], c["kc"], c["vc"], c["bt"], c["cl"], SCALE, 16,
+                                k_scales=c["ks"], v_scales=c["vs"]) for i in range(2)]
+        host_cl = c["cl"].cpu()
+        torch.cuda.synchronize()
+        events = [None, None]
+        for k in range(4):
+            i = k & 1
+            if events[i] is not None:
+                events[i].synchronize()
+            with torch.cuda.stream(streams[i]):
+                dq[i].copy_(hq[k], non_blocking=True)
+                plans[i].run(host_context_lens=host_cl)
+                hout[k].copy_(dout[i], non_blocking=True)
+                events[i] = torch.cuda.Event()
+                events[i].record()
+        torch.cuda.synchronize()
+        for k in range(4):
+            assert torch.equal(hout[k], refs[k]), (kind, k)
+        assert ops.read_status(c["q"].device) == 0
