@@ -610,6 +610,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   uint2 qc[NS], qd[NS];
   uint4 ra[NS], rb[NS];  // q rows fetched ahead of the piece that uses them
   float qsc0 = 0.f, qsc1 = 0.f;
+  // Per-token logit factors besides the K scale: scale * log2 e, times s_q for INT8.
+  float qks0 = qs, qks1 = qs;
   int q_b = -1, q_seg = -1;
 
   auto fetch_q = [&](int b, int seg) {
@@ -686,8 +688,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   auto convert_q = [&]() {
     if constexpr (I8) {
       split_row(ra, qa, qc, qsc0);
+      qks0 = qs * qsc0;  // s_q is a power of two: exact
       if constexpr (GT == 16) {
         split_row(rb, qb, qd, qsc1);
+        qks1 = qs * qsc1;
       } else {
 #pragma unroll
         for (int si = 0; si < NS; ++si) {
@@ -957,8 +961,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       float x[4], y[4];
       if constexpr (I8) {
         // Three exact integer dot products per (head, token) on the raw K bytes, combined as
-        // s_q (p1 + p2/128 + p3/16384).
-        constexpr float k2 = 1.f / 128.f, k3 = 1.f / 16384.f;
+        // p1 + (128 p2 + p3) / 16384 (|q2|, |q3| <= 64, so |128 p2 + p3| < 2^28 is exact in
+        // int32; s_q multiplies in with the K scale below).
+        constexpr float k3 = 1.f / 16384.f;
         if constexpr (NT == 1) {
           // Eight heads leave the MMA's rows 8-15 free: they take q's second part, so one MMA
           // gives p1 (rows g) and p2 (rows g+8) and a second one p3.
@@ -983,9 +988,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           for (int jt = 0; jt < 2; ++jt)
 #pragma unroll
             for (int e = 0; e < 2; ++e)
-              x[2 * jt + e] = fmaf((float)s3[jt][e], k3,
-                                   fmaf((float)s12[jt][2 + e], k2, (float)s12[jt][e])) *
-                              qsc0;
+              x[2 * jt + e] = fmaf((float)(s12[jt][2 + e] * 128 + s3[jt][e]), k3,
+                                   (float)s12[jt][e]);
           y[0] = y[1] = y[2] = y[3] = 0.f;
         } else {
           int sa[2][4], sb2[2][4], sc3[2][4];
@@ -1009,18 +1013,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                          k8[si][jt].y);
             }
           }
-          auto comb = [&](int jt, int e, float qsc) {
-            return fmaf((float)sc3[jt][e], k3,
-                        fmaf((float)sb2[jt][e], k2, (float)sa[jt][e])) * qsc;
+          auto comb = [&](int jt, int e) {
+            return fmaf((float)(sb2[jt][e] * 128 + sc3[jt][e]), k3, (float)sa[jt][e]);
           };
-          x[0] = comb(0, 0, qsc0);
-          x[1] = comb(0, 1, qsc0);
-          x[2] = comb(1, 0, qsc0);
-          x[3] = comb(1, 1, qsc0);
-          y[0] = comb(0, 2, qsc1);
-          y[1] = comb(0, 3, qsc1);
-          y[2] = comb(1, 2, qsc1);
-          y[3] = comb(1, 3, qsc1);
+          x[0] = comb(0, 0);
+          x[1] = comb(0, 1);
+          x[2] = comb(1, 0);
+          x[3] = comb(1, 1);
+          y[0] = comb(0, 2);
+          y[1] = comb(0, 3);
+          y[2] = comb(1, 2);
+          y[3] = comb(1, 3);
         }
       } else {
         if constexpr (F8) {
@@ -1061,18 +1064,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         y[2] = sacc[1][0][2] + sacc[1][1][2];
         y[3] = sacc[1][0][3] + sacc[1][1][3];
       }
-      // Logits in log2 units.
-      float ksc[4] = {qs, qs, qs, qs};
-      if constexpr (BYTE) {
-        ksc[0] = ksv.x * qs;
-        ksc[1] = ksv.y * qs;
-        ksc[2] = ksv.z * qs;
-        ksc[3] = ksv.w * qs;
-      }
+      // Logits in log2 units: per token, the K scale times scale * log2 e (and, INT8, times
+      // the q part scale s_q of the row's head, qks0 / qks1).
+      {
+        const float kx[4] = {ksv.x, ksv.y, ksv.z, ksv.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        x[e] *= ksc[e];
-        if constexpr (NT == 2) y[e] *= ksc[e];
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (BYTE) {
+            x[e] *= kx[e] * qks0;
+            if constexpr (NT == 2) y[e] *= kx[e] * qks1;
+          } else {
+            x[e] *= qs;
+            if constexpr (NT == 2) y[e] *= qs;
+          }
+        }
       }
       if (valid < kSubTokens) {
 #pragma unroll
