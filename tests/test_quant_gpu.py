@@ -367,3 +367,53 @@ def test_prefill_input_dtypes_bit_exact(source, int8):
                                                  bt, nb, bs)
     assert np.array_equal(kc.cpu().numpy().view(np.uint8), okc.view(np.uint8))
     assert np.array_equal(vc.cpu().numpy().view(np.uint8), ovc.view(np.uint8))
+
+
+@pytest.mark.parametrize("kind", ["i8", "fp8", "f16"])
+def test_large_token_write_bit_exact(kind):
+    """A large token-granular write (1.32 M rows: 330,000 tokens x 2 kv heads x K and V, a
+    grid of 165,000 CTAs) in a shuffled slot order with padding tokens, bit-exact with the
+    oracle for INT8 (values and scales), FP8 (e4m3 bytes and scales) and the FP16 copy."""
+    N, KVH, bs = 330_000, 2, 16
+    g = gen.Gen(41)
+    k = gen.kv_values(g, (N, KVH, 128), "lognormal_outlier").astype(np.float16)
+    v = gen.kv_values(g, (N, KVH, 128), "normal").astype(np.float16)
+    nb = (N + bs - 1) // bs + 5
+    slots = gen.Gen(42).permutation(nb * bs)[:N].astype(np.int32)
+    slots[::977] = -1  # padding tokens: skipped
+    dt = {"i8": torch.int8, "fp8": torch.float8_e4m3fn, "f16": torch.float16}[kind]
+    kc = torch.zeros(nb, KVH, 16, bs, 8, dtype=torch.uint8 if kind == "fp8" else dt,
+                     device="cuda")
+    vc = torch.zeros(nb, KVH, 128, bs, dtype=kc.dtype, device="cuda")
+    if kind == "fp8":
+        kc, vc = kc.view(dt), vc.view(dt)
+    ks = torch.zeros(nb, KVH, bs, dtype=torch.float32, device="cuda")
+    vs = torch.zeros_like(ks)
+    tk, tv, ts = to_cuda(k, v, slots)
+    if kind == "f16":
+        _ops().write_into_cache(tk, tv, kc, vc, ts, bs)
+        kq, vq = k, v
+    else:
+        _ops().quantize_into_cache(tk, tv, kc, vc, ks, vs, ts, bs)
+        if kind == "i8":
+            kq, ksc = pa_oracle.quantize_per_token(k, "f16")
+            vq, vsc = pa_oracle.quantize_per_token(v, "f16")
+        else:
+            kq, ksc = pa_oracle.quantize_per_token_fp8(k)
+            vq, vsc = pa_oracle.quantize_per_token_fp8(v)
+    _ops().check_status(tk.device)
+    m = slots >= 0
+    blk, off = slots[m] // bs, slots[m] % bs
+    okc = np.zeros((nb, KVH, 16, bs, 8), kq.dtype)
+    ovc = np.zeros((nb, KVH, 128, bs), vq.dtype)
+    okc[blk, :, :, off, :] = kq[m].reshape(-1, KVH, 16, 8)
+    ovc[blk, :, :, off] = vq[m]
+    u = np.uint16 if kind == "f16" else np.uint8
+    assert np.array_equal(kc.view(torch.uint8).cpu().numpy().view(u), okc.view(u))
+    assert np.array_equal(vc.view(torch.uint8).cpu().numpy().view(u), ovc.view(u))
+    if kind != "f16":
+        oks = np.zeros((nb, KVH, bs), np.float32)
+        ovs = np.zeros((nb, KVH, bs), np.float32)
+        oks[blk, :, off] = ksc[m]
+        ovs[blk, :, off] = vsc[m]
+        assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
