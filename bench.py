@@ -762,9 +762,10 @@ def run_config(torch, name, args, rank, world, device, dist, peak, soak_ms=0.0):
 
 def write_kernels(torch, device, peak, steps):
     """The cache-write kernels alone at config 3's bulk size (64 x 8192 tokens, 2 kv heads):
-    the token-granular quantize-write (one row per warp) and the block-granular prefill
-    scatter. Algorithmic bytes per (token, kv head): 2 x 128 x 2 B read, 2 x 128 B + 2 x 4 B
-    written."""
+    the token-granular quantize-write through slot_mapping (at this size the windowed kernel,
+    whose aligned runs of 16 slots, here every sequence's blocks, take the grouped page
+    stores) and the block-granular prefill scatter. Algorithmic bytes per (token, kv head):
+    2 x 128 x 2 B read, 2 x 128 B + 2 x 4 B written."""
     from pa_b200 import ops
     S, L, KVH = 64, 8192, 2
     N = S * L
@@ -791,7 +792,7 @@ def write_kernels(torch, device, peak, steps):
     out = {}
     for label, fn, kern in (
             ("quantize_into_cache", lambda: ops.quantize_into_cache(
-                k2, v2, kc, vc, ks, vs, slots, BLOCK), "write_rows_kernel"),
+                k2, v2, kc, vc, ks, vs, slots, BLOCK), "write_slots_kernel"),
             ("prefill_into_cache", lambda: ops.prefill_into_cache(
                 k, v, kc, vc, bt, cl, BLOCK, k_scales=ks, v_scales=vs), "prefill_kernel")):
         g = capture(torch, fn, reps, 3, cap)

@@ -92,14 +92,14 @@ struct RowQ {
   float s;
 };
 
+// The row quantiser on values already loaded: each lane holds x = its D/32 consecutive values
+// of the row (T is the input dtype, which the per-token scale is rounded to).
 template <typename T, int KIND, int D>
-__device__ __forceinline__ RowQ<KIND, D> warp_quantize_row(const T* src, int lane,
-                                                           const float* fix) {
+__device__ __forceinline__ RowQ<KIND, D> warp_quantize_vals(const float (&x)[D / 32],
+                                                            const float* fix) {
   constexpr int DPL = D / 32;
   static_assert(DPL % 4 == 0, "a lane packs whole 32-bit words");
   RowQ<KIND, D> r;
-  float x[DPL];
-  load_vals<T, DPL>(src + lane * DPL, x);
   if constexpr (KIND == kRowsF16) {
     r.s = 0.f;
 #pragma unroll
@@ -137,6 +137,14 @@ __device__ __forceinline__ RowQ<KIND, D> warp_quantize_row(const T* src, int lan
     r.s = s;
   }
   return r;
+}
+
+template <typename T, int KIND, int D>
+__device__ __forceinline__ RowQ<KIND, D> warp_quantize_row(const T* src, int lane,
+                                                           const float* fix) {
+  float x[D / 32];
+  load_vals<T, D / 32>(src + lane * (D / 32), x);
+  return warp_quantize_vals<T, KIND, D>(x, fix);
 }
 
 // Element e (0 <= e < D/32) of lane `lane`'s part of a quantised row, as stored.

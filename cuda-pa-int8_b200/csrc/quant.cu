@@ -207,6 +207,129 @@ __host__ __device__ constexpr int prefill_stage_bytes() {
   return 2 * 16 * D * (int)sizeof(T);
 }
 
+// Quantise (or round to fp16) one page's 16-token group and store it into the page layout.
+// raw[t]: the lane's four consecutive input values (head_dim 4 lane .. 4 lane + 3) of token t of
+// the group, zero at and past `valid`; the group starts at token offset g0 (a multiple of 16)
+// of page row `page` (= block * kv_heads + kv_head). INT8 (I8) quantises per token, or with the
+// fixed scale kfix / vfix when given, and writes the scales; otherwise the values are rounded to
+// fp16. Rows at and past `valid` are written as zeros (INT8: scale 0).
+//   K page [D/8][bs][8]: the lane pair (2c, 2c+1) owns 8-wide chunk c; after the pair swaps
+//     half of its words, lane 2c writes the group's tokens 0-7 and lane 2c+1 tokens 8-15;
+//   V page [D][bs]: lane l owns head_dim rows 4l..4l+3, 16 consecutive tokens each.
+template <typename T, bool I8, int D>
+__device__ __forceinline__ void store_group(const typename Raw4<T>::type (&raw)[16], bool is_v,
+                                            int valid, size_t page, int g0, int bs,
+                                            void* k_cache, void* v_cache, float* k_scales,
+                                            float* v_scales, const float* kfix,
+                                            const float* vfix, int lane) {
+  static_assert(D == 128, "a lane holds four consecutive head_dim values");
+  constexpr unsigned kAll = 0xffffffffu;
+  constexpr int ELEM = I8 ? 1 : 2;
+  constexpr int KW = I8 ? 1 : 2;  // words of a lane's four values: int8 one, fp16 two
+  const int c = lane >> 1;   // K: the lane pair's 8-wide chunk
+  const int hlf = lane & 1;  // K: which half of the chunk the lane holds
+  uint8_t* pg =
+      reinterpret_cast<uint8_t*>(is_v ? v_cache : k_cache) + page * (size_t)D * bs * ELEM;
+  // Per token, the lane's four values as stored: int8 bytes (zero past the context) or fp16.
+  uint32_t kw[16][KW];
+  if constexpr (I8) {
+    // Row maxima, reduced together: after the steps over lane masks 16, 8, 4, 2 lane l holds
+    // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it.
+    float m[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float x[4];
+      unpack4(raw[t], static_cast<const T*>(nullptr), x);
+      m[t] = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    }
+#pragma unroll
+    for (int h = 8, msk = 16; h >= 1; h >>= 1, msk >>= 1) {
+      const bool up = (lane & msk) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const float send = up ? m[i] : m[i + h];
+        const float keep = up ? m[i + h] : m[i];
+        m[i] = fmaxf(keep, __shfl_xor_sync(kAll, send, msk));
+      }
+    }
+    const float am = fmaxf(m[0], __shfl_xor_sync(kAll, m[0], 1));
+    const int row = lane >> 1;
+    const float* fix = is_v ? vfix : kfix;
+    float s = 0.f;
+    if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
+    const float inv = __frcp_rn(s);
+    if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
+    // The clamp can bind only with a fixed scale or a scale below 2^-14 (fp16 subnormal).
+    const bool ranged = __any_sync(kAll, fix != nullptr || (s > 0.f && s < 0x1p-14f));
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const float st = __shfl_sync(kAll, s, 2 * t);
+      const float it = __shfl_sync(kAll, inv, 2 * t);
+      float x[4];
+      unpack4(raw[t], static_cast<const T*>(nullptr), x);
+      kw[t][0] = t < valid ? quant4<false>(x, st, f2_pack(it, it), ranged) : 0u;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float x[4];
+      unpack4(raw[t], static_cast<const T*>(nullptr), x);
+      kw[t][0] = half2_bits(x[0], x[1]);
+      kw[t][1] = half2_bits(x[2], x[3]);
+    }
+  }
+  if (!is_v) {
+    // The pair swaps half of its words: lane 2c keeps tokens 0-7 and receives its partner's
+    // words for them, lane 2c+1 the same for tokens 8-15.
+    uint32_t pw[8][KW];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int w = 0; w < KW; ++w)
+        pw[i][w] = __shfl_xor_sync(kAll, hlf ? kw[i][w] : kw[8 + i][w], 1);
+    uint8_t* dst = pg + ((size_t)c * bs + g0 + 8 * hlf) * 8 * ELEM;
+#pragma unroll
+    for (int i = 0; i < 8; i += (I8 ? 2 : 1)) {
+      if constexpr (I8) {
+        // Two tokens of 8 bytes: lane 2c's half of the chunk, then lane 2c+1's.
+        const uint32_t a0 = hlf ? pw[i][0] : kw[i][0], a1 = hlf ? kw[8 + i][0] : pw[i][0];
+        const uint32_t b0 = hlf ? pw[i + 1][0] : kw[i + 1][0];
+        const uint32_t b1 = hlf ? kw[9 + i][0] : pw[i + 1][0];
+        *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(a0, a1, b0, b1);
+      } else {
+        // One token of 16 bytes.
+        const uint32_t l0 = hlf ? pw[i][0] : kw[i][0], l1 = hlf ? pw[i][1] : kw[i][1];
+        const uint32_t h0 = hlf ? kw[8 + i][0] : pw[i][0], h1 = hlf ? kw[8 + i][1] : pw[i][1];
+        *reinterpret_cast<uint4*>(dst + i * 16) = make_uint4(l0, l1, h0, h1);
+      }
+    }
+  } else {
+    // Per head_dim row 4 * lane + e, the group's 16 tokens: byte (int8) or half (fp16) e of
+    // every token's word.
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint32_t vw[4 * KW];
+#pragma unroll
+      for (int u = 0; u < 4 * KW; ++u) {
+        if constexpr (I8) {
+          const uint32_t sel = (uint32_t)e | ((uint32_t)(4 + e) << 4);
+          vw[u] = __byte_perm(__byte_perm(kw[4 * u][0], kw[4 * u + 1][0], sel),
+                              __byte_perm(kw[4 * u + 2][0], kw[4 * u + 3][0], sel), 0x5410);
+        } else {
+          // Halves e of tokens 2u and 2u + 1.
+          const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+          vw[u] = __byte_perm(kw[2 * u][e >> 1], kw[2 * u + 1][e >> 1], sel);
+        }
+      }
+      uint8_t* dst = pg + ((size_t)(4 * lane + e) * bs + g0) * ELEM;
+#pragma unroll
+      for (int u = 0; u < KW; ++u)
+        *reinterpret_cast<uint4*>(dst + 16 * u) =
+            make_uint4(vw[4 * u], vw[4 * u + 1], vw[4 * u + 2], vw[4 * u + 3]);
+    }
+  }
+}
+
 template <typename T, bool I8, int D>
 __global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int S, int L, int KVH,
@@ -216,16 +339,11 @@ __global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
     const float* __restrict__ vfix, int* status) {
   static_assert(D == 128, "a lane holds four consecutive head_dim values");
   using R = typename Raw4<T>::type;
-  constexpr unsigned kAll = 0xffffffffu;
-  constexpr int ELEM = I8 ? 1 : 2;
-  constexpr int KW = I8 ? 1 : 2;  // words of a lane's four values: int8 one, fp16 two
   constexpr int SB = prefill_stage_bytes<T, D>();
   constexpr int ROWB = D * (int)sizeof(T);
   extern __shared__ __align__(16) uint8_t psm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* stage0 = psm + (size_t)warp * 2 * SB;
-  const int c = lane >> 1;   // K: the lane pair's 8-wide chunk
-  const int hlf = lane & 1;  // K: which half of the chunk the lane holds
   const int gpb = bs / 16;   // groups per block
   const int cap = min(L, max_blocks * bs);
   const size_t tstride = (size_t)KVH * D;
@@ -288,109 +406,8 @@ __global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
 
   // Quantise (or round to fp16) and store one page's 16-token group from its raw rows.
   auto page_group = [&](const R (&raw)[16], bool is_v, const Grp& gr) {
-    const int g0 = gr.t0 % bs;
-    const int valid = gr.valid;
-    const size_t page = (size_t)gr.blk * KVH + gr.kvh;
-    uint8_t* pg =
-        reinterpret_cast<uint8_t*>(is_v ? v_cache : k_cache) + page * (size_t)D * bs * ELEM;
-    // Per token, the lane's four values as stored: int8 bytes (zero past the context) or fp16.
-    uint32_t kw[16][KW];
-    if constexpr (I8) {
-      // Row maxima, reduced together: after the steps over lane masks 16, 8, 4, 2 lane l holds
-      // the maximum of row (l >> 1) over its half of the lanes; mask 1 completes it.
-      float m[16];
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        float x[4];
-        unpack4(raw[t], static_cast<const T*>(nullptr), x);
-        m[t] = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-      }
-#pragma unroll
-      for (int h = 8, msk = 16; h >= 1; h >>= 1, msk >>= 1) {
-        const bool up = (lane & msk) != 0;
-#pragma unroll
-        for (int i = 0; i < h; ++i) {
-          const float send = up ? m[i] : m[i + h];
-          const float keep = up ? m[i + h] : m[i];
-          m[i] = fmaxf(keep, __shfl_xor_sync(kAll, send, msk));
-        }
-      }
-      const float am = fmaxf(m[0], __shfl_xor_sync(kAll, m[0], 1));
-      const int row = lane >> 1;
-      const float* fix = is_v ? vfix : kfix;
-      float s = 0.f;
-      if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
-      const float inv = __frcp_rn(s);
-      if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
-      // The clamp can bind only with a fixed scale or a scale below 2^-14 (fp16 subnormal).
-      const bool ranged = __any_sync(kAll, fix != nullptr || (s > 0.f && s < 0x1p-14f));
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const float st = __shfl_sync(kAll, s, 2 * t);
-        const float it = __shfl_sync(kAll, inv, 2 * t);
-        float x[4];
-        unpack4(raw[t], static_cast<const T*>(nullptr), x);
-        kw[t][0] = t < valid ? quant4<false>(x, st, f2_pack(it, it), ranged) : 0u;
-      }
-    } else {
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        float x[4];
-        unpack4(raw[t], static_cast<const T*>(nullptr), x);
-        kw[t][0] = half2_bits(x[0], x[1]);
-        kw[t][1] = half2_bits(x[2], x[3]);
-      }
-    }
-    if (!is_v) {
-      // The pair swaps half of its words: lane 2c keeps tokens 0-7 and receives its partner's
-      // words for them, lane 2c+1 the same for tokens 8-15.
-      uint32_t pw[8][KW];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int w = 0; w < KW; ++w)
-          pw[i][w] = __shfl_xor_sync(kAll, hlf ? kw[i][w] : kw[8 + i][w], 1);
-      uint8_t* dst = pg + ((size_t)c * bs + g0 + 8 * hlf) * 8 * ELEM;
-#pragma unroll
-      for (int i = 0; i < 8; i += (I8 ? 2 : 1)) {
-        if constexpr (I8) {
-          // Two tokens of 8 bytes: lane 2c's half of the chunk, then lane 2c+1's.
-          const uint32_t a0 = hlf ? pw[i][0] : kw[i][0], a1 = hlf ? kw[8 + i][0] : pw[i][0];
-          const uint32_t b0 = hlf ? pw[i + 1][0] : kw[i + 1][0];
-          const uint32_t b1 = hlf ? kw[9 + i][0] : pw[i + 1][0];
-          *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(a0, a1, b0, b1);
-        } else {
-          // One token of 16 bytes.
-          const uint32_t l0 = hlf ? pw[i][0] : kw[i][0], l1 = hlf ? pw[i][1] : kw[i][1];
-          const uint32_t h0 = hlf ? kw[8 + i][0] : pw[i][0], h1 = hlf ? kw[8 + i][1] : pw[i][1];
-          *reinterpret_cast<uint4*>(dst + i * 16) = make_uint4(l0, l1, h0, h1);
-        }
-      }
-    } else {
-      // Per head_dim row 4 * lane + e, the group's 16 tokens: byte (int8) or half (fp16) e of
-      // every token's word.
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        uint32_t vw[4 * KW];
-#pragma unroll
-        for (int u = 0; u < 4 * KW; ++u) {
-          if constexpr (I8) {
-            const uint32_t sel = (uint32_t)e | ((uint32_t)(4 + e) << 4);
-            vw[u] = __byte_perm(__byte_perm(kw[4 * u][0], kw[4 * u + 1][0], sel),
-                                __byte_perm(kw[4 * u + 2][0], kw[4 * u + 3][0], sel), 0x5410);
-          } else {
-            // Halves e of tokens 2u and 2u + 1.
-            const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
-            vw[u] = __byte_perm(kw[2 * u][e >> 1], kw[2 * u + 1][e >> 1], sel);
-          }
-        }
-        uint8_t* dst = pg + ((size_t)(4 * lane + e) * bs + g0) * ELEM;
-#pragma unroll
-        for (int u = 0; u < KW; ++u)
-          *reinterpret_cast<uint4*>(dst + 16 * u) =
-              make_uint4(vw[4 * u], vw[4 * u + 1], vw[4 * u + 2], vw[4 * u + 3]);
-      }
-    }
+    store_group<T, I8, D>(raw, is_v, gr.valid, (size_t)gr.blk * KVH + gr.kvh, gr.t0 % bs, bs,
+                          k_cache, v_cache, k_scales, v_scales, kfix, vfix, lane);
   };
   // The group's K (which = 0) or V rows of stage st, zeros past the context.
   auto read_rows = [&](int st, int which, int valid, R (&raw)[16]) {
@@ -440,6 +457,103 @@ __global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
+// Token-granular write of many tokens (a prefill through slot_mapping). Tokens whose slots
+// form an aligned run of 16 (slots s, s+1, ..., s+15 with s a multiple of 16, so all in one
+// block when the block size is a multiple of 16) are written as one group with the prefill's
+// 16-byte page stores; the other tokens row by row. Warp (window, kv head, K|V) takes the
+// 16 tokens [t0, t0 + 16) of its window: from the slots of tokens t0 - 16 .. t0 + 47 it marks
+// the tokens that head a run (heads are at least 16 tokens apart, so at most one lies in the
+// window), writes the run headed inside its window, and writes the rows of its window's
+// tokens that no run covers (token t is covered when t - slot % 16 heads a run). Those rows
+// are all requested before the first is quantised.
+// ---------------------------------------------------------------------------------------
+template <typename T, bool I8, int D>
+__global__ void __launch_bounds__(256) write_slots_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
+    const int* __restrict__ slot_mapping, int N, int KVH, void* __restrict__ k_cache,
+    void* __restrict__ v_cache, float* __restrict__ k_scales, float* __restrict__ v_scales,
+    int NB, int bs, const float* __restrict__ kfix, const float* __restrict__ vfix,
+    int* status) {
+  using R = typename Raw4<T>::type;
+  constexpr int KIND = I8 ? kRowsI8 : kRowsF16;
+  constexpr unsigned kAll = 0xffffffffu;
+  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long nwin = ((long long)N + 15) >> 4;
+  if (gw >= nwin * KVH * 2) return;
+  const int which = (int)(gw & 1);  // 0: K, 1: V
+  const long long wk = gw >> 1;
+  const int kvh = (int)(wk % KVH);
+  const long long t0 = (wk / KVH) << 4;
+  auto slot_at = [&](long long u) -> int {
+    return (u >= 0 && u < N) ? __ldg(slot_mapping + u) : -1;
+  };
+  // a: slot of token t0 - 16 + lane; b: slot of token t0 + 16 + lane.
+  const int a = slot_at(t0 - 16 + lane);
+  const int b = slot_at(t0 + 16 + lane);
+  int a1 = __shfl_down_sync(kAll, a, 1);
+  const int b0 = __shfl_sync(kAll, b, 0);
+  if (lane == 31) a1 = b0;
+  const int b1 = __shfl_down_sync(kAll, b, 1);
+  // Bit j of links: token t0 - 16 + j's slot is followed by the next slot.
+  const unsigned la = __ballot_sync(kAll, a >= 0 && a1 == a + 1);
+  const unsigned lb = __ballot_sync(kAll, lane < 31 && b >= 0 && b1 == b + 1);
+  const unsigned long long links = (unsigned long long)la | ((unsigned long long)lb << 32);
+  // Bit j of heads: token t0 - 16 + j heads an aligned run of 16.
+  const bool head = a >= 0 && (a & 15) == 0 && ((links >> lane) & 0x7fffull) == 0x7fffull;
+  const unsigned heads = __ballot_sync(kAll, head);
+  // Bit i of covered: window token t0 + i lies in a run (its head among t0 + i - 15 .. t0 + i).
+  const unsigned covered =
+      __ballot_sync(kAll, lane < 16 && ((heads >> (lane + 1)) & 0xffffu) != 0u);
+  const T* src = (which ? v : k) + (size_t)kvh * D + lane * 4;
+
+  const unsigned own = heads >> 16;
+  if (own != 0u) {
+    const int i = __ffs(own) - 1;
+    const int s0 = __shfl_sync(kAll, a, 16 + i);
+    const int blk = s0 / bs;
+    if (blk >= NB) {
+      if (lane == 0) flag_error(status, PA_ERR_SLOT);
+    } else {
+      R raw[16];
+      const T* p = src + (t0 + i) * token_stride;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) raw[t] = load_raw4(p + t * token_stride);
+      store_group<T, I8, D>(raw, which != 0, 16, (size_t)blk * KVH + kvh, s0 - blk * bs, bs,
+                            k_cache, v_cache, k_scales, v_scales, kfix, vfix, lane);
+    }
+  }
+
+  unsigned todo = ~covered & 0xffffu;
+  const long long left = (long long)N - t0;
+  if (left < 16) todo &= (1u << left) - 1u;
+  if (todo == 0u) return;
+  R raw[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t)
+    raw[t] = ((todo >> t) & 1u) ? load_raw4(src + (t0 + t) * token_stride) : R{};
+  void* cache = which ? v_cache : k_cache;
+  float* scales = which ? v_scales : k_scales;
+  const float* fix = which ? vfix : kfix;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    if (!((todo >> t) & 1u)) continue;
+    const int s = __shfl_sync(kAll, a, 16 + t);
+    if (s < 0) continue;  // padding token
+    const int blk = s / bs;
+    if (blk >= NB) {
+      if (lane == 0) flag_error(status, PA_ERR_SLOT);
+      continue;
+    }
+    float x[4];
+    unpack4(raw[t], static_cast<const T*>(nullptr), x);
+    const RowQ<KIND, D> q = warp_quantize_vals<T, KIND, D>(x, fix);
+    store_row<KIND, D>(q, lane, which != 0, cache, scales, (size_t)blk * KVH + kvh,
+                       s - blk * bs, bs);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
 // Per-tensor absmax -> scale.
 // ---------------------------------------------------------------------------------------
 template <typename T>
@@ -467,6 +581,12 @@ __global__ void scale_finalize_kernel(const unsigned int* amax_bits, float* scal
   *scale_out = s;
 }
 
+// Token-granular writes use the windowed kernel when it has at least this many warps per SM
+// (a warp walks up to 16 rows that no run covers one after another, so fewer warps would leave
+// scattered writes, a decode step's appends, waiting on that walk); smaller writes take one
+// warp per row.
+constexpr int kSlotWindowMinWarpsPerSm = 32;
+
 template <typename T>
 cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long long ts,
                           const int* slots, int N, int KVH, void* kc, void* vc, float* ks,
@@ -478,6 +598,29 @@ cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long lo
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
   if (D != 128) return cudaErrorInvalidValue;
+  // Many tokens, block size a multiple of 16 and rows aligned for the lanes' vector loads: the
+  // windowed write, whose aligned runs of 16 slots take the page-group stores.
+  constexpr size_t kRaw = sizeof(typename Raw4<T>::type);
+  const bool aligned = reinterpret_cast<uintptr_t>(k) % kRaw == 0 &&
+                       reinterpret_cast<uintptr_t>(v) % kRaw == 0 &&
+                       ((size_t)ts * sizeof(T)) % kRaw == 0;
+  const long long wwarps = ((long long)N + 15) / 16 * KVH * 2;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  if (kind != kRowsFP8 && wwarps >= (long long)sms * kSlotWindowMinWarpsPerSm && bs % 16 == 0 &&
+      aligned) {
+    const int wgrid = (int)((wwarps + 7) / 8);
+    if (kind == kRowsI8) {
+      write_slots_kernel<T, true, 128><<<wgrid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
+                                                              ks, vs, NB, bs, kf, vf, status);
+    } else {
+      write_slots_kernel<T, false, 128><<<wgrid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc,
+                                                               vc, ks, vs, NB, bs, kf, vf, status);
+    }
+    return cudaGetLastError();
+  }
   if (kind == kRowsFP8) {
     write_rows_kernel<T, kRowsFP8, 128><<<grid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
                                                               ks, vs, NB, bs, nullptr, nullptr,

@@ -417,3 +417,96 @@ def test_large_token_write_bit_exact(kind):
         oks[blk, :, off] = ksc[m]
         ovs[blk, :, off] = vsc[m]
         assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
+
+
+def _prefill_slots(rng, S, bs, nb_extra=3, pad_every=0):
+    """Slots of a flattened prefill batch: S sequences of random lengths, some continuing at a
+    position inside a block (chunked prefill), each through its own shuffled block table, with
+    padding tokens (-1) between some sequences. Returns (slots, num_blocks)."""
+    lens = rng.integers(1, 700, S)
+    starts = np.where(rng.random(S) < 0.4, rng.integers(0, 3 * bs, S), 0)
+    nblk = [(st + ln + bs - 1) // bs for st, ln in zip(starts, lens)]
+    nb = int(sum(nblk)) + nb_extra
+    perm = rng.permutation(nb).astype(np.int64)
+    out, used = [], 0
+    for st, ln, m in zip(starts, lens, nblk):
+        bt = perm[used:used + m]
+        used += m
+        p = np.arange(st, st + ln)
+        out.append((bt[p // bs] * bs + p % bs).astype(np.int32))
+        if rng.random() < 0.3:
+            out.append(np.full(rng.integers(1, 5), -1, np.int32))
+    return np.concatenate(out), nb
+
+
+def _oracle_slots(k, v, slots, nb, KVH, bs, kind, in_dtype, k_fix=None, v_fix=None):
+    """Expected caches (and scales) after the token-granular write of k, v at slots."""
+    if kind == "f16":
+        kq, vq = k.astype(np.float16), v.astype(np.float16)
+        ksc = vsc = None
+    elif k_fix is not None:
+        kq = pa_oracle.quantize_with_scale(k.astype(np.float32), k_fix)
+        vq = pa_oracle.quantize_with_scale(v.astype(np.float32), v_fix)
+        ksc = np.full(k.shape[:-1], k_fix, np.float32)
+        vsc = np.full(v.shape[:-1], v_fix, np.float32)
+    else:
+        kq, ksc = pa_oracle.quantize_per_token(k, in_dtype)
+        vq, vsc = pa_oracle.quantize_per_token(v, in_dtype)
+    m = slots >= 0
+    blk, off = slots[m] // bs, slots[m] % bs
+    okc = np.zeros((nb, KVH, 16, bs, 8), kq.dtype)
+    ovc = np.zeros((nb, KVH, 128, bs), vq.dtype)
+    okc[blk, :, :, off, :] = kq[m].reshape(-1, KVH, 16, 8)
+    ovc[blk, :, :, off] = vq[m]
+    if ksc is None:
+        return okc, ovc, None, None
+    oks = np.zeros((nb, KVH, bs), np.float32)
+    ovs = np.zeros((nb, KVH, bs), np.float32)
+    oks[blk, :, off] = ksc[m]
+    ovs[blk, :, off] = vsc[m]
+    return okc, ovc, oks, ovs
+
+
+@pytest.mark.parametrize("kind,in_dtype,bs,fixed", [
+    ("i8", "f16", 16, False), ("i8", "bf16", 32, False), ("i8", "f32", 16, False),
+    ("i8", "f16", 16, True), ("f16", "f16", 16, False), ("f16", "f32", 32, False),
+    ("i8", "f16", 8, False)])
+def test_prefill_through_slots_bit_exact(kind, in_dtype, bs, fixed):
+    """A prefill batch written through slot_mapping (vLLM-style): tokens of one sequence have
+    consecutive slots inside its blocks, so aligned runs of 16 take the grouped page stores
+    and the rest (sequence ends, chunked-prefill starts inside a block, block size 8) the
+    row path. Values and scales bit-exact with the oracle for int8 (per-token or fixed
+    scales) and fp16 caches, fp16 / bf16 / fp32 input rows."""
+    rng = np.random.default_rng(51 + bs)
+    slots, nb = _prefill_slots(rng, 60, bs)
+    N, KVH = slots.shape[0], 4
+    # Large enough for the windowed write (at least 32 of its warps per SM).
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert (N + 15) // 16 * KVH * 2 >= 32 * sms
+    g = gen.Gen(52)
+    k = gen.kv_values(g, (N, KVH, 128), "lognormal_outlier").astype(np.float32)
+    v = gen.kv_values(g, (N, KVH, 128), "normal").astype(np.float32)
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[in_dtype]
+    tk = torch.from_numpy(k).to(tdt).cuda()
+    tv = torch.from_numpy(v).to(tdt).cuda()
+    # The oracle sees the rows as the kernel does: rounded to the input dtype.
+    k, v = tk.float().cpu().numpy(), tv.float().cpu().numpy()
+    ts = torch.from_numpy(slots).cuda()
+    kc, vc, ks, vs = _caches(nb, KVH, bs, int8=(kind == "i8"))
+    kfix = vfix = None
+    if kind == "f16":
+        _ops().write_into_cache(tk, tv, kc, vc, ts, bs)
+    elif fixed:
+        kfix, vfix = np.float32(0.093), np.float32(0.021)
+        _ops().quantize_into_cache(tk, tv, kc, vc, ks, vs, ts, bs,
+                                   k_scale=torch.tensor(kfix, device="cuda"),
+                                   v_scale=torch.tensor(vfix, device="cuda"))
+    else:
+        _ops().quantize_into_cache(tk, tv, kc, vc, ks, vs, ts, bs)
+    _ops().check_status(tk.device)
+    okc, ovc, oks, ovs = _oracle_slots(k, v, slots, nb, KVH, bs, kind, in_dtype, kfix, vfix)
+    u = np.uint16 if kind == "f16" else np.uint8
+    assert np.array_equal(kc.cpu().numpy().view(u), okc.view(u))
+    assert np.array_equal(vc.cpu().numpy().view(u), ovc.view(u))
+    if oks is not None:
+        assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
