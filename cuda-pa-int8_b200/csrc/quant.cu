@@ -78,22 +78,25 @@ __global__ void __launch_bounds__(256) step_rows_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
-// Block-granular prefill. The work is cut into 16-token groups of one (sequence, block,
-// kv-head); every group of a block inside the context is written, and tokens past the
-// context in a sequence's last block are written as zeros with scale 0. CTAs are persistent
-// (as many as fit on the GPU) and each warp walks its share of the groups with a two-deep
-// pipeline: while it works on one group, the next group's K and V rows are copied into its
-// shared-memory buffer by cp.async (each lane copies, and later reads, only its own four
-// head_dim values of each row). For a group a lane holds four consecutive head_dim values of
-// each of the 16 rows, the warp reduces the 16 row maxima together, and the lane writes the
-// quantised (or fp16) values straight into the page layout with 16-byte stores:
-//   K page [D/8][bs][8]: the lane pair (2c, 2c+1) owns 8-wide chunk c; after the pair swaps
-//     half of its words, lane 2c writes the group's tokens 0-7 and lane 2c+1 tokens 8-15;
-//   V page [D][bs]: lane l owns head_dim rows 4l..4l+3, 16 consecutive tokens each.
+// Group writes (the block-granular prefill scatter and the runs of the windowed token write):
+// a warp holds the 16 rows of one 16-token group of one page, each lane four consecutive
+// head_dim values of every row, loaded straight into registers; the warp reduces the 16 row
+// maxima together and the lane writes the quantised (or fp16) values into the page layout with
+// 16-byte stores (store_group below).
 // ---------------------------------------------------------------------------------------
-constexpr int kPrefillThreads = 128;
-constexpr int kPrefillWarps = kPrefillThreads / 32;
-constexpr int kLensSmem = 1024;  // sequence lengths staged in shared memory
+// CTA shape of the group-write kernels (prefill_kernel, write_slots_kernel): threads, and the
+// CTAs per SM their register budget is compiled for. Both kernels are bound by the latency of
+// a group's dependent steps, so resident warps count: five CTAs of four warps (96 registers)
+// measured 17 % faster on the windowed write than two CTAs of eight warps (116 registers);
+// six CTAs spill.
+#ifndef PA_GROUP_THREADS
+#define PA_GROUP_THREADS 128
+#endif
+#ifndef PA_GROUP_MIN_CTAS
+#define PA_GROUP_MIN_CTAS 5
+#endif
+constexpr int kGroupThreads = PA_GROUP_THREADS;
+constexpr int kGroupWarps = kGroupThreads / 32;
 
 // A lane's four consecutive input values as loaded (8 bytes for 16-bit inputs, 16 for fp32).
 template <typename T> struct Raw4 { using type = uint2; };
@@ -185,26 +188,6 @@ __device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, uint64_
                        0x5410);
   return ((uint32_t)(uint8_t)quant1(x[0], s)) | ((uint32_t)(uint8_t)quant1(x[1], s) << 8) |
          ((uint32_t)(uint8_t)quant1(x[2], s) << 16) | ((uint32_t)(uint8_t)quant1(x[3], s) << 24);
-}
-
-// cp.async of one lane's four input values (8 or 16 bytes).
-template <typename T>
-__device__ __forceinline__ void cp_async_raw4(void* smem_dst, const T* gsrc) {
-  if constexpr (sizeof(T) == 2) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)),
-                 "l"(gsrc)
-                 : "memory");
-  } else {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
-                 "l"(gsrc)
-                 : "memory");
-  }
-}
-
-// Shared memory of one warp's pipeline stage: 16 K rows then 16 V rows of D values.
-template <typename T, int D>
-__host__ __device__ constexpr int prefill_stage_bytes() {
-  return 2 * 16 * D * (int)sizeof(T);
 }
 
 // Quantise (or round to fp16) one page's 16-token group and store it into the page layout.
@@ -330,129 +313,68 @@ __device__ __forceinline__ void store_group(const typename Raw4<T>::type (&raw)[
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Block-granular prefill over the work items (sequence, block, 16-token group of the block,
+// kv head, K|V): an item inside the context writes that group of its sequence's block; tokens
+// past the context in a sequence's last block are written as zeros (INT8: scale 0); items of
+// blocks past the context are skipped. CTAs are persistent (as many as fit on the GPU) and
+// warps stride over the items; a warp that reaches a sequence's items past its context moves
+// straight on to the next sequence, so block tables sized for long contexts cost little. An
+// item's rows inside the context are all requested before the first is processed.
+// ---------------------------------------------------------------------------------------
 template <typename T, bool I8, int D>
-__global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
+__global__ void __launch_bounds__(kGroupThreads, PA_GROUP_MIN_CTAS) prefill_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int S, int L, int KVH,
     const int* __restrict__ block_table, const int* __restrict__ context_lens, int max_blocks,
     void* __restrict__ k_cache, void* __restrict__ v_cache, float* __restrict__ k_scales,
     float* __restrict__ v_scales, int NB, int bs, const float* __restrict__ kfix,
     const float* __restrict__ vfix, int* status) {
-  static_assert(D == 128, "a lane holds four consecutive head_dim values");
   using R = typename Raw4<T>::type;
-  constexpr int SB = prefill_stage_bytes<T, D>();
-  constexpr int ROWB = D * (int)sizeof(T);
-  extern __shared__ __align__(16) uint8_t psm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* stage0 = psm + (size_t)warp * 2 * SB;
-  const int gpb = bs / 16;   // groups per block
+  const int lane = threadIdx.x & 31;
+  const int gpb = bs / 16;  // groups per block
+  // A sequence's items, in the order (block, group, kv head, K|V): those of blocks inside the
+  // context come first.
+  const long long per_seq = (long long)max_blocks * gpb * KVH * 2;
+  const long long total = (long long)S * per_seq;
+  const long long first = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
   const int cap = min(L, max_blocks * bs);
   const size_t tstride = (size_t)KVH * D;
-  const long long total = (long long)S * KVH * max_blocks * gpb;
-  const long long W = (long long)gridDim.x * kPrefillWarps;
-
-  // Group g of the flattened (sequence, kv-head, block, group) space, when it is to be
-  // written (its block lies inside the context): sequence, kv head, first token, rows inside
-  // the context (<= 0 for a group past the context in the last block), page row.
-  // The sequences' lengths, clamped to the buffers, in shared memory (the first kLensSmem;
-  // later ones are read from global memory).
-  int* s_ctx = reinterpret_cast<int*>(psm + (size_t)kPrefillWarps * 2 * SB);
-  for (int i = threadIdx.x; i < min(S, kLensSmem); i += kPrefillThreads) {
-    int ctx = __ldg(context_lens + i);
+  const bool narrow = total <= 0xffffffffLL;  // 32-bit division suffices
+  for (long long gw = first; gw < total; gw += nw) {
+    const int b = narrow ? (int)((unsigned)gw / (unsigned)per_seq) : (int)(gw / per_seq);
+    const int item = (int)(gw - (long long)b * per_seq);
+    int ctx = __ldg(context_lens + b);
     if (ctx > cap) {
-      if (blockIdx.x == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
+      if (lane == 0 && item == 0) flag_error(status, PA_ERR_CONTEXT_RANGE);
       ctx = cap;
     }
-    s_ctx[i] = ctx < 0 ? 0 : ctx;
-  }
-  __syncthreads();
-  auto ctx_of = [&](int b) -> int {
-    if (b < kLensSmem) return s_ctx[b];
-    const int ctx = __ldg(context_lens + b);
-    return ctx > cap ? cap : (ctx < 0 ? 0 : ctx);
-  };
-  // A group to write: sequence, kv head, first token, rows inside the context (<= 0 for a
-  // group past the context in the last block) and its block id, loaded here and first used
-  // when the group is processed, one pipeline step later.
-  struct Grp {
-    int b, kvh, t0, valid, blk;
-  };
-  auto decode_grp = [&](long long g, Grp& r) -> bool {
-    const int jg = (int)(g % ((long long)max_blocks * gpb));
-    const long long bk = g / ((long long)max_blocks * gpb);
-    r.kvh = (int)(bk % KVH);
-    r.b = (int)(bk / KVH);
-    const int j = jg / gpb;
-    r.t0 = j * bs + (jg - j * gpb) * 16;
-    const int ctx = ctx_of(r.b);
-    if (j >= (ctx + bs - 1) / bs) return false;  // past the sequence's last block
-    r.valid = min(16, ctx - r.t0);
-    r.blk = __ldg(block_table + (size_t)r.b * max_blocks + j);
-    return true;
-  };
-  // Copy the group's rows inside the context into stage st (one commit group).
-  auto issue = [&](const Grp& gr, int st) {
-    uint8_t* sb = stage0 + st * SB + lane * 4 * (int)sizeof(T);
-    const size_t base = ((size_t)gr.b * L * KVH + gr.kvh) * D + lane * 4;
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      if (t < gr.valid) {
-        const size_t off = base + (size_t)(gr.t0 + t) * tstride;
-        cp_async_raw4(sb + t * ROWB, k + off);
-        cp_async_raw4(sb + (16 + t) * ROWB, v + off);
-      }
+    if (ctx < 0) ctx = 0;
+    if (item >= (ctx + bs - 1) / bs * gpb * KVH * 2) {
+      // Past the sequence's last block: on to this warp's first item of the next sequence
+      // (the items a warp takes are those congruent to `first` modulo nw).
+      const long long next = (long long)(b + 1) * per_seq;
+      gw = next + (((first - next) % nw) + nw) % nw - nw;
+      continue;
     }
-    cp_async_commit();
-  };
-
-  // Quantise (or round to fp16) and store one page's 16-token group from its raw rows.
-  auto page_group = [&](const R (&raw)[16], bool is_v, const Grp& gr) {
-    store_group<T, I8, D>(raw, is_v, gr.valid, (size_t)gr.blk * KVH + gr.kvh, gr.t0 % bs, bs,
-                          k_cache, v_cache, k_scales, v_scales, kfix, vfix, lane);
-  };
-  // The group's K (which = 0) or V rows of stage st, zeros past the context.
-  auto read_rows = [&](int st, int which, int valid, R (&raw)[16]) {
-    const uint8_t* sb = stage0 + st * SB + which * 16 * ROWB + lane * 4 * (int)sizeof(T);
+    const int which = item & 1;  // 0: K, 1: V
+    const int kvh = (item >> 1) % KVH;
+    const int jg = (item >> 1) / KVH;
+    const int j = jg / gpb;
+    const int t0 = j * bs + (jg - j * gpb) * 16;
+    const int valid = min(16, ctx - t0);
+    const int blk = __ldg(block_table + (size_t)b * max_blocks + j);
+    if (blk < 0 || blk >= NB) {
+      if (lane == 0) flag_error(status, PA_ERR_BLOCK_ID);
+      continue;
+    }
+    const T* src = (which ? v : k) + ((size_t)b * L * KVH + kvh) * D + lane * 4;
+    R raw[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t)
-      raw[t] = t < valid ? *reinterpret_cast<const R*>(sb + t * ROWB) : R{};
-  };
-
-  // The groups to write, in this warp's share of the flattened space.
-  long long g = (long long)blockIdx.x * kPrefillWarps + warp;
-  auto next_grp = [&](Grp& out) -> bool {
-    while (g < total) {
-      const bool ok = decode_grp(g, out);
-      g += W;
-      if (ok) return true;
-    }
-    return false;
-  };
-  Grp cur, nxt;
-  bool have = next_grp(cur);
-  if (have) issue(cur, 0);
-  int st = 0;
-  while (have) {
-    const bool more = next_grp(nxt);
-    if (more) {
-      issue(nxt, st ^ 1);
-      cp_async_wait_group_1();
-    } else {
-      cp_async_wait_all();
-    }
-    __syncwarp();
-    if (cur.blk >= 0 && cur.blk < NB) {
-      R raw[16];
-      read_rows(st, 0, cur.valid, raw);
-      page_group(raw, false, cur);
-      read_rows(st, 1, cur.valid, raw);
-      page_group(raw, true, cur);
-    } else if (lane == 0) {
-      flag_error(status, PA_ERR_BLOCK_ID);
-    }
-    __syncwarp();  // the stage's rows are read before the next issue overwrites it
-    cur = nxt;
-    have = more;
-    st ^= 1;
+      raw[t] = t < valid ? load_raw4(src + (size_t)(t0 + t) * tstride) : R{};
+    store_group<T, I8, D>(raw, which != 0, valid, (size_t)blk * KVH + kvh, t0 % bs, bs, k_cache,
+                          v_cache, k_scales, v_scales, kfix, vfix, lane);
   }
 }
 
@@ -468,7 +390,7 @@ __global__ void __launch_bounds__(kPrefillThreads) prefill_kernel(
 // are all requested before the first is quantised.
 // ---------------------------------------------------------------------------------------
 template <typename T, bool I8, int D>
-__global__ void __launch_bounds__(256) write_slots_kernel(
+__global__ void __launch_bounds__(kGroupThreads, PA_GROUP_MIN_CTAS) write_slots_kernel(
     const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
     const int* __restrict__ slot_mapping, int N, int KVH, void* __restrict__ k_cache,
     void* __restrict__ v_cache, float* __restrict__ k_scales, float* __restrict__ v_scales,
@@ -611,13 +533,13 @@ cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long lo
   if (e != cudaSuccess) return e;
   if (kind != kRowsFP8 && wwarps >= (long long)sms * kSlotWindowMinWarpsPerSm && bs % 16 == 0 &&
       aligned) {
-    const int wgrid = (int)((wwarps + 7) / 8);
+    const int wgrid = (int)((wwarps + kGroupWarps - 1) / kGroupWarps);
     if (kind == kRowsI8) {
-      write_slots_kernel<T, true, 128><<<wgrid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc, vc,
-                                                              ks, vs, NB, bs, kf, vf, status);
+      write_slots_kernel<T, true, 128><<<wgrid, kGroupThreads, 0, st>>>(
+          kk, vv, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf, vf, status);
     } else {
-      write_slots_kernel<T, false, 128><<<wgrid, 256, 0, st>>>(kk, vv, ts, slots, N, KVH, kc,
-                                                               vc, ks, vs, NB, bs, kf, vf, status);
+      write_slots_kernel<T, false, 128><<<wgrid, kGroupThreads, 0, st>>>(
+          kk, vv, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf, vf, status);
     }
     return cudaGetLastError();
   }
@@ -667,21 +589,20 @@ cudaError_t launch_prefill_t(bool i8, const void* k, const void* v, int S, int L
   const T* kk = static_cast<const T*>(k);
   const T* vv = static_cast<const T*>(v);
   auto kern = i8 ? prefill_kernel<T, true, 128> : prefill_kernel<T, false, 128>;
-  // Persistent CTAs: as many as fit on the GPU, never more than there are groups.
-  const int smem = kPrefillWarps * 2 * prefill_stage_bytes<T, 128>() + kLensSmem * 4;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  // Persistent CTAs: as many as fit on the GPU, never more than the work items need.
   int dev = 0, sms = 0, per_sm = 0;
-  e = cudaGetDevice(&dev);
+  cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e == cudaSuccess)
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPrefillThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGroupThreads, 0);
   if (e != cudaSuccess) return e;
-  const long long groups = (long long)S * KVH * max_blocks * (bs / 16);
-  const long long want = (groups + kPrefillWarps - 1) / kPrefillWarps;
-  const int grid = (int)std::min<long long>(want, (long long)sms * std::max(per_sm, 1));
-  kern<<<grid, kPrefillThreads, smem, st>>>(kk, vv, S, L, KVH, bt, cl, max_blocks, kc, vc, ks,
-                                            vs, NB, bs, kf, vf, status);
+  const long long per_seq = (long long)max_blocks * (bs / 16) * KVH * 2;
+  if (per_seq > 0x7fffffffLL) return cudaErrorInvalidValue;  // items of a sequence are ints
+  const long long items = (long long)S * per_seq;
+  const int grid = (int)std::min<long long>((items + kGroupWarps - 1) / kGroupWarps,
+                                             (long long)sms * std::max(per_sm, 1));
+  kern<<<grid, kGroupThreads, 0, st>>>(kk, vv, S, L, KVH, bt, cl, max_blocks, kc, vc, ks, vs, NB,
+                                       bs, kf, vf, status);
   return cudaGetLastError();
 }
 

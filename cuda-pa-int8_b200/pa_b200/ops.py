@@ -584,8 +584,8 @@ def write_into_cache(key, value, k_cache, v_cache, slot_mapping, block_size=16):
 def prefill_into_cache(k, v, k_cache, v_cache, block_table, context_lens, block_size=16, *,
                        k_scales=None, v_scales=None, k_scale=None, v_scale=None):
     """Bulk write of contiguous per-sequence K/V [num_seqs, max_len, kv_heads, head_dim] into
-    the blocks listed by block_table (persistent warps over 16-token groups, the next group's
-    rows copied while the current one is written; 16-byte stores into the page layout). INT8
+    the blocks listed by block_table (a warp per 16-token group of one page, K or V, its rows
+    loaded into registers together; 16-byte stores into the page layout). INT8
     caches are quantised per token (or with k_scale/v_scale); FP16 caches get a copy.
     Tokens past a sequence's context inside its last block are written as zeros."""
     _require(k.is_cuda and v.is_cuda, "tensors must be on CUDA")
