@@ -117,10 +117,6 @@ __device__ __forceinline__ void cp_async_commit() {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
-// All but the most recent commit group complete.
-__device__ __forceinline__ void cp_async_wait_group_1() {
-  asm volatile("cp.async.wait_group 1;" ::: "memory");
-}
 
 // Hint: bring the 128-byte line holding p into this SM's L1.
 __device__ __forceinline__ void prefetch_l1(const void* p) {
