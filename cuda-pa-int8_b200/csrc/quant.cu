@@ -193,13 +193,14 @@ __device__ __forceinline__ uint32_t quant4(const float (&x)[4], float s, uint64_
 // Quantise (or round to fp16) one page's 16-token group and store it into the page layout.
 // raw[t]: the lane's four consecutive input values (head_dim 4 lane .. 4 lane + 3) of token t of
 // the group, zero at and past `valid`; the group starts at token offset g0 (a multiple of 16)
-// of page row `page` (= block * kv_heads + kv_head). INT8 (I8) quantises per token, or with the
-// fixed scale kfix / vfix when given, and writes the scales; otherwise the values are rounded to
-// fp16. Rows at and past `valid` are written as zeros (INT8: scale 0).
+// of page row `page` (= block * kv_heads + kv_head). One-byte caches (I8) get per-token int8
+// (or, with kfix / vfix, the fixed scales) or, with F8, per-token e4m3 (scale = amax / 448, as
+// the row quantiser), and their scales; otherwise the values are rounded to fp16. Rows at and
+// past `valid` are written as zeros (one-byte caches: scale 0).
 //   K page [D/8][bs][8]: the lane pair (2c, 2c+1) owns 8-wide chunk c; after the pair swaps
 //     half of its words, lane 2c writes the group's tokens 0-7 and lane 2c+1 tokens 8-15;
 //   V page [D][bs]: lane l owns head_dim rows 4l..4l+3, 16 consecutive tokens each.
-template <typename T, bool I8, int D>
+template <typename T, bool I8, int D, bool F8 = false>
 __device__ __forceinline__ void store_group(const typename Raw4<T>::type (&raw)[16], bool is_v,
                                             int valid, size_t page, int g0, int bs,
                                             void* k_cache, void* v_cache, float* k_scales,
@@ -237,20 +238,40 @@ __device__ __forceinline__ void store_group(const typename Raw4<T>::type (&raw)[
     }
     const float am = fmaxf(m[0], __shfl_xor_sync(kAll, m[0], 1));
     const int row = lane >> 1;
-    const float* fix = is_v ? vfix : kfix;
-    float s = 0.f;
-    if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
-    const float inv = __frcp_rn(s);
-    if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
-    // The clamp can bind only with a fixed scale or a scale below 2^-14 (fp16 subnormal).
-    const bool ranged = __any_sync(kAll, fix != nullptr || (s > 0.f && s < 0x1p-14f));
+    if constexpr (F8) {
+      const float s = row < valid ? __fdiv_rn(am, 448.f) : 0.f;
+      if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const float st = __shfl_sync(kAll, s, 2 * t);
-      const float it = __shfl_sync(kAll, inv, 2 * t);
-      float x[4];
-      unpack4(raw[t], static_cast<const T*>(nullptr), x);
-      kw[t][0] = t < valid ? quant4<false>(x, st, f2_pack(it, it), ranged) : 0u;
+      for (int t = 0; t < 16; ++t) {
+        const float st = __shfl_sync(kAll, s, 2 * t);
+        float x[4];
+        unpack4(raw[t], static_cast<const T*>(nullptr), x);
+        uint32_t w = 0u;
+        if (st > 0.f) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w |= (uint32_t)(uint8_t)__nv_cvt_float_to_fp8(__fdiv_rn(x[e], st), __NV_SATFINITE,
+                                                          __NV_E4M3)
+                 << (8 * e);
+        }
+        kw[t][0] = w;
+      }
+    } else {
+      const float* fix = is_v ? vfix : kfix;
+      float s = 0.f;
+      if (row < valid) s = fix != nullptr ? __ldg(fix) : token_scale<T>(am);
+      const float inv = __frcp_rn(s);
+      if (hlf == 0) (is_v ? v_scales : k_scales)[page * bs + g0 + row] = s;
+      // The clamp can bind only with a fixed scale or a scale below 2^-14 (fp16 subnormal).
+      const bool ranged = __any_sync(kAll, fix != nullptr || (s > 0.f && s < 0x1p-14f));
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const float st = __shfl_sync(kAll, s, 2 * t);
+        const float it = __shfl_sync(kAll, inv, 2 * t);
+        float x[4];
+        unpack4(raw[t], static_cast<const T*>(nullptr), x);
+        kw[t][0] = t < valid ? quant4<false>(x, st, f2_pack(it, it), ranged) : 0u;
+      }
     }
   } else {
 #pragma unroll
@@ -389,7 +410,7 @@ __global__ void __launch_bounds__(kGroupThreads, PA_GROUP_MIN_CTAS) prefill_kern
 // tokens that no run covers (token t is covered when t - slot % 16 heads a run). Those rows
 // are all requested before the first is quantised.
 // ---------------------------------------------------------------------------------------
-template <typename T, bool I8, int D>
+template <typename T, int KIND, int D>
 __global__ void __launch_bounds__(kGroupThreads, PA_GROUP_MIN_CTAS) write_slots_kernel(
     const T* __restrict__ k, const T* __restrict__ v, long long token_stride,
     const int* __restrict__ slot_mapping, int N, int KVH, void* __restrict__ k_cache,
@@ -397,7 +418,7 @@ __global__ void __launch_bounds__(kGroupThreads, PA_GROUP_MIN_CTAS) write_slots_
     int NB, int bs, const float* __restrict__ kfix, const float* __restrict__ vfix,
     int* status) {
   using R = typename Raw4<T>::type;
-  constexpr int KIND = I8 ? kRowsI8 : kRowsF16;
+  constexpr bool BYTE = KIND != kRowsF16;  // one-byte cache with scales
   constexpr unsigned kAll = 0xffffffffu;
   const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -441,8 +462,9 @@ __global__ void __launch_bounds__(kGroupThreads, PA_GROUP_MIN_CTAS) write_slots_
       const T* p = src + (t0 + i) * token_stride;
 #pragma unroll
       for (int t = 0; t < 16; ++t) raw[t] = load_raw4(p + t * token_stride);
-      store_group<T, I8, D>(raw, which != 0, 16, (size_t)blk * KVH + kvh, s0 - blk * bs, bs,
-                            k_cache, v_cache, k_scales, v_scales, kfix, vfix, lane);
+      store_group<T, BYTE, D, KIND == kRowsFP8>(raw, which != 0, 16, (size_t)blk * KVH + kvh,
+                                                s0 - blk * bs, bs, k_cache, v_cache, k_scales,
+                                                v_scales, kfix, vfix, lane);
     }
   }
 
@@ -531,14 +553,16 @@ cudaError_t launch_rows_t(int kind, int D, const void* k, const void* v, long lo
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  if (kind != kRowsFP8 && wwarps >= (long long)sms * kSlotWindowMinWarpsPerSm && bs % 16 == 0 &&
-      aligned) {
+  if (wwarps >= (long long)sms * kSlotWindowMinWarpsPerSm && bs % 16 == 0 && aligned) {
     const int wgrid = (int)((wwarps + kGroupWarps - 1) / kGroupWarps);
-    if (kind == kRowsI8) {
-      write_slots_kernel<T, true, 128><<<wgrid, kGroupThreads, 0, st>>>(
+    if (kind == kRowsFP8) {
+      write_slots_kernel<T, kRowsFP8, 128><<<wgrid, kGroupThreads, 0, st>>>(
+          kk, vv, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, nullptr, nullptr, status);
+    } else if (kind == kRowsI8) {
+      write_slots_kernel<T, kRowsI8, 128><<<wgrid, kGroupThreads, 0, st>>>(
           kk, vv, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf, vf, status);
     } else {
-      write_slots_kernel<T, false, 128><<<wgrid, kGroupThreads, 0, st>>>(
+      write_slots_kernel<T, kRowsF16, 128><<<wgrid, kGroupThreads, 0, st>>>(
           kk, vv, ts, slots, N, KVH, kc, vc, ks, vs, NB, bs, kf, vf, status);
     }
     return cudaGetLastError();

@@ -444,6 +444,9 @@ def _oracle_slots(k, v, slots, nb, KVH, bs, kind, in_dtype, k_fix=None, v_fix=No
     if kind == "f16":
         kq, vq = k.astype(np.float16), v.astype(np.float16)
         ksc = vsc = None
+    elif kind == "fp8":
+        kq, ksc = pa_oracle.quantize_per_token_fp8(k)
+        vq, vsc = pa_oracle.quantize_per_token_fp8(v)
     elif k_fix is not None:
         kq = pa_oracle.quantize_with_scale(k.astype(np.float32), k_fix)
         vq = pa_oracle.quantize_with_scale(v.astype(np.float32), v_fix)
@@ -470,13 +473,13 @@ def _oracle_slots(k, v, slots, nb, KVH, bs, kind, in_dtype, k_fix=None, v_fix=No
 @pytest.mark.parametrize("kind,in_dtype,bs,fixed", [
     ("i8", "f16", 16, False), ("i8", "bf16", 32, False), ("i8", "f32", 16, False),
     ("i8", "f16", 16, True), ("f16", "f16", 16, False), ("f16", "f32", 32, False),
-    ("i8", "f16", 8, False)])
+    ("i8", "f16", 8, False), ("fp8", "f16", 16, False), ("fp8", "bf16", 32, False)])
 def test_prefill_through_slots_bit_exact(kind, in_dtype, bs, fixed):
     """A prefill batch written through slot_mapping (vLLM-style): tokens of one sequence have
     consecutive slots inside its blocks, so aligned runs of 16 take the grouped page stores
     and the rest (sequence ends, chunked-prefill starts inside a block, block size 8) the
     row path. Values and scales bit-exact with the oracle for int8 (per-token or fixed
-    scales) and fp16 caches, fp16 / bf16 / fp32 input rows."""
+    scales), fp8 (e4m3) and fp16 caches, fp16 / bf16 / fp32 input rows."""
     rng = np.random.default_rng(51 + bs)
     slots, nb = _prefill_slots(rng, 60, bs)
     N, KVH = slots.shape[0], 4
@@ -492,7 +495,9 @@ def test_prefill_through_slots_bit_exact(kind, in_dtype, bs, fixed):
     # The oracle sees the rows as the kernel does: rounded to the input dtype.
     k, v = tk.float().cpu().numpy(), tv.float().cpu().numpy()
     ts = torch.from_numpy(slots).cuda()
-    kc, vc, ks, vs = _caches(nb, KVH, bs, int8=(kind == "i8"))
+    kc, vc, ks, vs = _caches(nb, KVH, bs, int8=(kind != "f16"))
+    if kind == "fp8":
+        kc, vc = kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn)
     kfix = vfix = None
     if kind == "f16":
         _ops().write_into_cache(tk, tv, kc, vc, ts, bs)
@@ -506,7 +511,8 @@ def test_prefill_through_slots_bit_exact(kind, in_dtype, bs, fixed):
     _ops().check_status(tk.device)
     okc, ovc, oks, ovs = _oracle_slots(k, v, slots, nb, KVH, bs, kind, in_dtype, kfix, vfix)
     u = np.uint16 if kind == "f16" else np.uint8
-    assert np.array_equal(kc.cpu().numpy().view(u), okc.view(u))
-    assert np.array_equal(vc.cpu().numpy().view(u), ovc.view(u))
+    kb, vb = (kc.view(torch.uint8), vc.view(torch.uint8)) if kind == "fp8" else (kc, vc)
+    assert np.array_equal(kb.cpu().numpy().view(u), okc.view(u))
+    assert np.array_equal(vb.cpu().numpy().view(u), ovc.view(u))
     if oks is not None:
         assert _bits_equal(ks, oks) and _bits_equal(vs, ovs)
