@@ -242,6 +242,11 @@ int pa_merge_partials(void* out, const float* partials, int num_parts, int num_s
  * negative slot skips the token. If k_fixed_scale / v_fixed_scale are non-null they point to
  * one device fp32 scale each (per-tensor mode, paged_cache.py:143-145) and that scale is
  * written into the scale slots instead. status (nullable) receives PA_ERR_SLOT bits.
+ * Large writes (about 19 K tokens x 2 kv heads and up on a B200) write every run of 16
+ * consecutive tokens whose slots are 16 consecutive slots starting at a multiple of 16 (a
+ * prefill's full 16-token groups, block_size a multiple of 16) with whole-group stores, several
+ * times faster than the row-by-row write that the other tokens, and small writes, take; the
+ * result is the same either way.
  * ---------------------------------------------------------------------------------- */
 int pa_quantize_into_cache(const void* k, const void* v, int in_dtype, int64_t token_stride,
                            const int32_t* slot_mapping, int num_tokens, int num_kv_heads,
